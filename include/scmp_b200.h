@@ -1,0 +1,194 @@
+/*
+ * scmp_b200.h -- C ABI of the B200 (sm_100a) stochastic-computing matmul.
+ *
+ * Drop-in native boundary for the reference package scmp_kernels
+ * (swalther06/scmp_kernels). The reference is Python + Triton; its path
+ * orchestrators and Triton launchers are what the functions below replace.
+ * Each declaration names the reference function it stands in for
+ * (file:line relative to the reference repository root).
+ *
+ * Conventions
+ *   - every function returns an int status (SCMP_OK or an SCMP_ERR_* code) and
+ *     never throws or aborts; scmp_last_error() gives a message for the
+ *     calling thread;
+ *   - all array pointers are device pointers owned by the caller unless the
+ *     parameter says "host"; nothing here allocates device memory except the
+ *     one-time error flag of scmp_device_error();
+ *   - work is enqueued on the given CUDA stream (a cudaStream_t passed as
+ *     void*; NULL is the legacy default stream) on the current device;
+ *   - float arithmetic follows the reference bit for bit: IEEE float32 with
+ *     round-to-nearest-even per operation and no contraction into FMA.
+ */
+#ifndef SCMP_B200_H
+#define SCMP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SCMP_ABI_VERSION 1
+
+enum scmp_status {
+  SCMP_OK = 0,
+  SCMP_ERR_INVALID_ARG = 1, /* maps to ValueError in the Python layer          */
+  SCMP_ERR_CUDA = 2,        /* a CUDA runtime call failed                      */
+  SCMP_ERR_TIMEOUT = 3,     /* a bounded device-side wait gave up             */
+  SCMP_ERR_UNSUPPORTED = 4, /* maps to NotImplementedError                     */
+  SCMP_ERR_WORKSPACE = 5    /* workspace missing or smaller than required      */
+};
+
+enum scmp_granularity { SCMP_PER_TENSOR = 0, SCMP_PER_ROW = 1, SCMP_PER_HEAD = 2 };
+enum scmp_mode { SCMP_BIPOLAR = 0, SCMP_UNIPOLAR = 1 };
+
+/* scmp_matmul_desc.flags */
+#define SCMP_FLAG_FORCE_SIMT 0x1 /* use the CUDA-core GEMM instead of tcgen05  */
+
+/*
+ * Enable-signal tables (the "RNG cache" kept resident in HBM).
+ *
+ * Replaces build_enable_tables / build_k_table_only and their kernels
+ * build_cum_indicator_kernel + compute_k_table_kernel
+ * (scmp_kernels/sc/kernels.py:712-759, 871-894, 102-169).
+ *
+ * Inputs are the prepared comparator sequences (prefix / Owen scramble /
+ * rescale already applied, kernels.py:673-704), deduplicated to distinct rows:
+ *   ra: (n_ra, L) int32   sequences of operand a ("q" side)
+ *   rb: (n_rb, L) int32   sequences of operand b ("k" side)
+ * Outputs, for v in [0, vcap]:
+ *   ktab:    (n_ra, vcap+1) int16   ktab[r][v] = #{t < L : ra[r][t] < v}
+ *   pattern: (n_rb, vcap+1, lp/32) uint32, bit t of row (r, v) set iff
+ *            t < L and rb[r][t] < v  (the comparator stream of b, bit-packed)
+ * lp >= L is the padded stream length (a multiple of 32). Every sequence value
+ * must be < vcap, so that boundaries >= vcap saturate (ktab = L, all bits set).
+ * The reference's cum_indicator[d][k][v] equals popcount(pattern[d][v] & (2^k - 1)).
+ */
+int scmp_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, int n_rb, int L, int lp,
+                      int vcap, int16_t* ktab, uint32_t* pattern, void* stream);
+
+/*
+ * One sc_matmul call: quantise both operands, run the integer SC-GEMM and the
+ * path's float32 epilogue into `out`.
+ *
+ * Replaces the dispatch of _sc_matmul_impl (scmp_kernels/sc/matmul.py:224-279)
+ * and the five path orchestrators it calls:
+ *   per_tensor            _sc_matmul_per_tensor + _sc_matmul_enable_triton
+ *                         (kernels.py:1053-1204; 3D: 1207-1226)
+ *   per_row               _sc_matmul_per_row + _sc_matmul_grouped_enable
+ *                         (kernels.py:1573-1707)
+ *   per_row, chunk_d > 0  _sc_matmul_per_row_mlp + _sc_matmul_bipolar_mlp_chunked
+ *                         (kernels.py:1443-1566, 1274-1383)
+ *   per_row, 3D           _sc_matmul_per_row_batched (kernels.py:1778-1895)
+ *   per_head              _sc_matmul_per_head_bipolar (kernels.py:440-585)
+ * with apply_smoothing (scmp_kernels/quant/smoothquant.py:96-126) fused into
+ * the quantisation when smooth_scales is non-NULL. No host synchronisation:
+ * the per-tensor ranges that the reference reads back with .item()
+ * (matmul.py:227-230) are reduced and turned into scales on the device.
+ */
+typedef struct scmp_matmul_desc {
+  int granularity;      /* enum scmp_granularity                                   */
+  int mode;             /* enum scmp_mode                                          */
+  int sc_prec;          /* p: q_max = 2^(p-1)-1 (bipolar) or 2^p-1 (unipolar)       */
+  int stoc_len;         /* L                                                       */
+  int rng_levels;       /* G, the resolved enable grid (2^p when rng_levels=None)  */
+  int chunk_d;          /* > 0 selects the chunked per_row path (2D bipolar, D > chunk_d) */
+  int group_a, group_b; /* per_row row-group sizes                                 */
+  int batch;            /* BH; 1 for 2D inputs                                     */
+  int n, m, d;          /* a: (batch, n, d), b: (batch, m, d), out: (batch, n, m)  */
+  const float* a;
+  const float* b;
+  const float* smooth_scales; /* (d,) or NULL                                      */
+  float* out;
+  const int16_t* ktab;     /* from scmp_build_tables                               */
+  const uint32_t* pattern; /* from scmp_build_tables                               */
+  const int32_t* amap;     /* (d,) table row of dimension j for operand a           */
+  const int32_t* bmap;     /* (d,) table row of dimension j for operand b           */
+  int vcap;                /* as passed to scmp_build_tables                       */
+  int lp;                  /* as passed to scmp_build_tables                       */
+  int flags;               /* SCMP_FLAG_*                                          */
+} scmp_matmul_desc;
+
+/* Bytes of device workspace scmp_sc_matmul needs for `desc` (host-only call). */
+int scmp_sc_matmul_workspace_size(const scmp_matmul_desc* desc, size_t* bytes);
+
+int scmp_sc_matmul(const scmp_matmul_desc* desc, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/*
+ * Enable-signal matmul on already-quantised operands.
+ * Replaces enable_matmul_triton + enable_matmul_tiled_kernel
+ * (scmp_kernels/sc/kernels.py:798-868, 176-252).
+ *   boundary_a (n, d) int16, boundary_b (m, d) int16, sign_a (n, d) int8 and
+ *   sign_b (m, d) int8 (signs ignored when is_bipolar == 0);
+ *   out (n, m) = fl32(S * fl32(q_max_sq / L)) with S the integer accumulator.
+ * Tables and maps as in scmp_matmul_desc. The workspace holds the signed
+ * thermometer lengths; scmp_enable_matmul_workspace_size gives its size.
+ */
+int scmp_enable_matmul_workspace_size(int n, int m, int d, size_t* bytes);
+int scmp_enable_matmul(const int16_t* ktab, const uint32_t* pattern, const int32_t* amap,
+                       const int32_t* bmap, int vcap, int L, int lp, const int16_t* boundary_a,
+                       const int16_t* boundary_b, const int8_t* sign_a, const int8_t* sign_b,
+                       int n, int m, int d, float q_max_sq, int is_bipolar, float* out,
+                       void* workspace, size_t workspace_bytes, int flags, void* stream);
+
+/*
+ * Quantisers with the reference's output formats (scmp_kernels/quant/).
+ *
+ * scmp_fused_quantize_bipolar        fused_quantize_bipolar, fused.py:162-189
+ *   boundary (rows, cols) int16, sign int8; *scale_out = (host double) the
+ *   scale max(abs_max, 1e-5) / q_max.
+ * scmp_fused_quantize_bipolar_perrow fused_quantize_bipolar_perrow, fused.py:134-159
+ *   per-row on-device scale written to scale_row (rows,) float32.
+ * scmp_fused_quantize_unipolar       fused_quantize_unipolar, fused.py:192-234
+ *   boundary int32; row_sum (rows,) float32 written when non-NULL
+ *   (compute_sum=True); *scale_out and *zp_out are host doubles.
+ * scmp_fused_quant_bipolar_batched   fused_quant_bipolar_batched_kernel, fused.py:237-283
+ *   x (bh, rows, cols); inv_scale (bh,) float32 device; outputs transposed
+ *   to (bh, cols, rows).
+ * scmp_grouped_symmetric_quant       _grouped_symmetric_quant, grouped.py:13-75
+ * scmp_grouped_asymmetric_quant      _grouped_asymmetric_quant, grouped.py:78-133
+ * scmp_grouped_symmetric_quant_batched  _grouped_symmetric_quant_batched, grouped.py:136-163
+ *   (group == 1 or group >= rows; any other group returns SCMP_ERR_UNSUPPORTED)
+ *   x_int is float32 like the reference's; sign int8 with 0 -> +1.
+ * The grouped quantisers need scratch: group_stats holds 3 floats per group.
+ */
+int scmp_fused_quantize_bipolar(const float* x, int rows, int cols, double abs_max, int sc_prec,
+                                int rng_levels, int16_t* boundary, int8_t* sign, double* scale_out,
+                                void* stream);
+int scmp_fused_quantize_bipolar_perrow(const float* x, int rows, int cols, int sc_prec,
+                                       int rng_levels, int16_t* boundary, int8_t* sign,
+                                       float* scale_row, void* stream);
+int scmp_fused_quantize_unipolar(const float* x, int rows, int cols, double fp_max, double fp_min,
+                                 int sc_prec, int rng_levels, int32_t* boundary, float* row_sum,
+                                 double* scale_out, double* zp_out, void* stream);
+int scmp_fused_quant_bipolar_batched(const float* x, int bh, int rows, int cols,
+                                     const float* inv_scale, int sc_prec, int rng_levels,
+                                     int16_t* boundary, int8_t* sign, void* stream);
+int scmp_grouped_symmetric_quant(const float* x, int batch, int rows, int cols, int group,
+                                 int q_max, float* scale_row, float* x_int, int8_t* sign,
+                                 float* group_stats, void* stream);
+int scmp_grouped_asymmetric_quant(const float* x, int rows, int cols, int group, int q_max,
+                                  float* scale_row, float* zp_row, float* x_int,
+                                  float* group_stats, void* stream);
+
+/* Profiling hook (no reference counterpart; the reference has no native
+ * timing). While set, scmp_sc_matmul and scmp_enable_matmul record the CUDA
+ * event gemm_start on their stream right before the SC-GEMM launch and
+ * gemm_stop right after it, so a caller can time the GEMM kernel alone. Both
+ * are cudaEvent_t passed as void*; NULL, NULL turns the hook off. Process-wide. */
+int scmp_set_profile_events(void* gemm_start, void* gemm_stop);
+
+/* Diagnostics. scmp_device_error synchronises the device, returns in *code
+ * the first error a kernel recorded since the last call (SCMP_OK if none)
+ * and clears it. */
+int scmp_device_error(int* code);
+const char* scmp_last_error(void);
+int scmp_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SCMP_B200_H */

@@ -1,0 +1,95 @@
+// Internal argument blocks shared by the quantisers, the GEMM kernels and the
+// C-ABI layer.
+#pragma once
+
+#include "common.cuh"
+
+namespace scmp {
+
+// Float32 epilogue recipes of the reference's path orchestrators. `raw` below
+// is fl32(S * inner) with inner = fl32(q_max^2 / L), the in-kernel scale of
+// enable_matmul_tiled_kernel (sc/kernels.py:212, 248).
+enum EpiKind {
+  EPI_RAW = 0,         // out = raw                               (enable_matmul_triton)
+  EPI_SCALAR = 1,      // out = raw * c0                          (per_tensor bipolar, kernels.py:1204)
+  EPI_SCALAR_UNI = 2,  // zero-point correction with host scalars (per_tensor unipolar, 1198-1204)
+  EPI_ROW = 3,         // out = raw * fl32(sa[r] * sb[c])         (per_row bipolar, 1707 / 1894)
+  EPI_ROW_UNI = 4,     // per-row zero-point correction           (per_row unipolar, 1699-1707)
+  EPI_HEAD = 5,        // out = S * fl32(inner * fl32(sa[bh]*sb[bh])) (per_head, 430-432, 550)
+  EPI_CHUNK = 6        // out += raw_c * fl32(sa_c[r] * sb_c[c])  (chunked, 1380-1381)
+};
+
+struct Epilogue {
+  int kind;
+  float inner;
+  const float* scal;  // EPI_SCALAR*: [0] c0 = fl32(scale_a*scale_b), [1] -zp_b, [2] zp_a, [3] fl32(D*zp_a*zp_b)
+  const float* sa;    // EPI_ROW*: (batch*n); EPI_CHUNK: (nchunks, n); EPI_HEAD: (batch)
+  const float* sb;    // EPI_ROW*: (batch*m); EPI_CHUNK: (nchunks, m); EPI_HEAD: (batch)
+  const float* zpa;   // EPI_ROW_UNI: (batch*n)
+  const float* zpb;   // EPI_ROW_UNI: (batch*m)
+  const float* asum;  // EPI_*_UNI: row sums of the quantised a (batch*n)
+  const float* bsum;  // EPI_*_UNI: row sums of the quantised b (batch*m)
+  float fd;           // EPI_ROW_UNI: float(D)
+};
+
+// Value of one output element for accumulation unit `unit` (chunk index for
+// EPI_CHUNK). ia / ib are row indices including the batch offset.
+__device__ __forceinline__ float epi_value(const Epilogue& e, int S, int ia, int ib, int bh,
+                                           int unit, int n, int m) {
+  const float Sf = (float)S;  // exact: |S| <= D * L < 2^24
+  if (e.kind == EPI_HEAD) return fmul(Sf, fmul(e.inner, fmul(e.sa[bh], e.sb[bh])));
+  const float raw = fmul(Sf, e.inner);
+  switch (e.kind) {
+    case EPI_SCALAR:
+      return fmul(raw, e.scal[0]);
+    case EPI_SCALAR_UNI: {
+      const float t1 = fmul(e.scal[1], e.asum[ia]);
+      const float t2 = fmul(e.scal[2], e.bsum[ib]);
+      const float t5 = fadd(fsub(t1, t2), e.scal[3]);
+      return fmul(fadd(raw, t5), e.scal[0]);
+    }
+    case EPI_ROW:
+      return fmul(raw, fmul(e.sa[ia], e.sb[ib]));
+    case EPI_ROW_UNI: {
+      const float zb = e.zpb[ib], za = e.zpa[ia];
+      const float t1 = fmul(-zb, e.asum[ia]);
+      const float t2 = fmul(za, e.bsum[ib]);
+      const float t4 = fmul(fmul(e.fd, za), zb);
+      const float t5 = fadd(fsub(t1, t2), t4);
+      return fmul(fadd(raw, t5), fmul(e.sa[ia], e.sb[ib]));
+    }
+    case EPI_CHUNK:
+      return fmul(raw, fmul(e.sa[(size_t)unit * n + ia], e.sb[(size_t)unit * m + ib]));
+    default:
+      return raw;
+  }
+}
+
+// SC-GEMM operands and epilogue.
+//   ka: (batch, n, d) int16, signed thermometer length sa * k of operand a;
+//   vb: (batch, m, d) int16, signed boundary sb * v of operand b;
+//   pattern/bmap: comparator streams of b, bit t of row (bmap[j], v);
+//   the d range is split into accumulation units of unit_d dimensions (the
+//   chunks of the chunked path; one unit of d otherwise).
+struct GemmArgs {
+  int batch, n, m, d;
+  int L, lp, vcap;
+  int bipolar;
+  const int16_t* ka;
+  const int16_t* vb;
+  const uint32_t* pattern;
+  const int32_t* bmap;
+  int unit_d;
+  float* out;
+  Epilogue epi;
+};
+
+// Host launchers (return cudaError_t of the launch).
+cudaError_t launch_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, int n_rb, int L,
+                                int lp, int vcap, int16_t* ktab, uint32_t* pattern,
+                                cudaStream_t st);
+cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t st);
+cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st);
+bool gemm_tc_supported(const GemmArgs& g);
+
+}  // namespace scmp

@@ -1,0 +1,327 @@
+// Quantisation prologue of the fused sc_matmul path (HBM-bound).
+//
+// Each kernel restates one of the reference's float32 quantisation recipes
+// bit for bit and writes the operands in the form the SC-GEMM consumes:
+//   operand a -> int16 sa * k, k = ktab[amap[j]][min(boundary, vcap)]
+//   operand b -> int16 sb * v, v = min(boundary, vcap)
+// (the reference keeps (boundary, sign) and looks k up inside the GEMM,
+// sc/kernels.py:229-231). SmoothQuant's a / s and b * s
+// (quant/smoothquant.py:124-126) are applied on the fly.
+#include "quant.cuh"
+
+namespace scmp {
+
+__device__ __forceinline__ float load_x(const QuantArgs& q, size_t row, int j) {
+  float x = __ldg(q.x + row * (size_t)q.d + j);
+  if (q.smooth) x = q.smooth_div ? fdiv(x, __ldg(q.smooth + j)) : fmul(x, __ldg(q.smooth + j));
+  return x;
+}
+
+__device__ __forceinline__ int16_t encode(const QuantArgs& q, int j, int boundary, float sgn) {
+  int v = boundary < q.vcap ? boundary : q.vcap;
+  if (q.ktab) v = __ldg(q.ktab + (size_t)__ldg(q.amap + j) * (q.vcap + 1) + v);
+  return (int16_t)(sgn < 0.f ? -v : v);
+}
+
+// --------------------------------------------------------------------------
+// statistics
+// --------------------------------------------------------------------------
+
+// stats[r] = {absmax, max, min} of (smoothed) row r; one warp per row.
+__global__ void row_stats_kernel(QuantArgs q, float* __restrict__ stats) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= q.rows) return;
+  float am = 0.f, mx = -INFINITY, mn = INFINITY;
+  for (int j = lane; j < q.d; j += 32) {
+    const float x = load_x(q, warp, j);
+    am = fmaxf(am, fabsf(x));
+    mx = fmaxf(mx, x);
+    mn = fminf(mn, x);
+  }
+  am = warp_max(am);
+  mx = warp_max(mx);
+  mn = warp_min(mn);
+  if (lane == 0) {
+    stats[3 * (size_t)warp + 0] = am;
+    stats[3 * (size_t)warp + 1] = mx;
+    stats[3 * (size_t)warp + 2] = mn;
+  }
+}
+
+// Reduce stats over the rows of one group: blockIdx.x = group.
+__device__ void group_reduce(const float* stats, int r0, int r1, float& am, float& mx, float& mn) {
+  __shared__ float sh[3][32];
+  __syncthreads();  // a previous call may still be reading sh
+  am = 0.f;
+  mx = -INFINITY;
+  mn = INFINITY;
+  for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+    am = fmaxf(am, stats[3 * (size_t)r]);
+    mx = fmaxf(mx, stats[3 * (size_t)r + 1]);
+    mn = fminf(mn, stats[3 * (size_t)r + 2]);
+  }
+  am = warp_max(am);
+  mx = warp_max(mx);
+  mn = warp_min(mn);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (l == 0) {
+    sh[0][w] = am;
+    sh[1][w] = mx;
+    sh[2][w] = mn;
+  }
+  __syncthreads();
+  if (w == 0) {
+    am = l < nw ? sh[0][l] : 0.f;
+    mx = l < nw ? sh[1][l] : -INFINITY;
+    mn = l < nw ? sh[2][l] : INFINITY;
+    am = warp_max(am);
+    mx = warp_max(mx);
+    mn = warp_min(mn);
+    if (l == 0) {
+      sh[0][0] = am;
+      sh[1][0] = mx;
+      sh[2][0] = mn;
+    }
+  }
+  __syncthreads();
+  am = sh[0][0];
+  mx = sh[1][0];
+  mn = sh[2][0];
+}
+
+// Group id layout: rows are (batch, rows_per_batch); inside a batch, full
+// groups of G rows and one remainder group; G >= rows_per_batch is one group
+// (quant/grouped.py:28-75).
+__device__ __forceinline__ void group_bounds(int g, int rpb, int G, int& r0, int& r1) {
+  const int gpb = G >= rpb ? 1 : cdiv(rpb, G);
+  const int b = g / gpb, gl = g % gpb;
+  if (G >= rpb) {
+    r0 = b * rpb;
+    r1 = r0 + rpb;
+  } else {
+    r0 = b * rpb + gl * G;
+    r1 = min(r0 + G, (b + 1) * rpb);
+  }
+}
+
+// Per-group scale (and zero point) written to every row of the group.
+//   symmetric  (grouped.py:46-47): scale = max(absmax, 1e-5) / q
+//   asymmetric (grouped.py:111-115): scale = max(max - min, 1e-5) / q,
+//              zp = clamp(round(-min / scale), 0, q)
+//   head       (kernels.py:490-495): scale = max(|max|, |min|, 1e-5) / q and
+//              inv = 1 / scale, one value per batch entry
+__global__ void group_params_kernel(const float* __restrict__ stats, int rpb, int G, int q,
+                                    int recipe, float* __restrict__ scale, float* __restrict__ zp) {
+  int r0, r1;
+  group_bounds(blockIdx.x, rpb, G, r0, r1);
+  float am, mx, mn;
+  group_reduce(stats, r0, r1, am, mx, mn);
+  const float qf = (float)q;
+  float sc = 0.f, z = 0.f;
+  if (recipe == GP_SYM) {
+    sc = fdiv(fmaxf(am, 1e-5f), qf);
+  } else if (recipe == GP_ASYM) {
+    sc = fdiv(fmaxf(fsub(mx, mn), 1e-5f), qf);
+    z = fclamp(frint(fdiv(-mn, sc)), 0.f, qf);
+  } else {  // GP_HEAD: per batch entry, scale in `scale`, inverse in `zp`
+    sc = fdiv(fmaxf(fmaxf(fabsf(mx), fabsf(mn)), 1e-5f), qf);
+    if (threadIdx.x == 0) {
+      scale[blockIdx.x] = sc;
+      zp[blockIdx.x] = fdiv(1.0f, sc);
+    }
+    return;
+  }
+  for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+    scale[r] = sc;
+    if (zp) zp[r] = z;
+  }
+}
+
+// Per-tensor parameters for both operands, computed in double like the
+// reference's host code (kernels.py:1173-1186, quant/fused.py:172-174, 204-209,
+// and the scale product of kernels.py:1204). One block of 1024 threads.
+//   scal[0] = fl32(scale_a * scale_b)        scal[4] = fl32(inv_scale_a)
+//   scal[1] = fl32(-zp_b)                    scal[5] = fl32(inv_scale_b)
+//   scal[2] = fl32(zp_a)                     scal[6] = fl32(zp_a)  (quant offset)
+//   scal[3] = fl32(D * zp_a * zp_b)          scal[7] = fl32(zp_b)
+__global__ void tensor_params_kernel(const float* __restrict__ stats_a, int rows_a,
+                                     const float* __restrict__ stats_b, int rows_b, int d, int q,
+                                     int unipolar, float* __restrict__ scal) {
+  float am_a, mx_a, mn_a, am_b, mx_b, mn_b;
+  group_reduce(stats_a, 0, rows_a, am_a, mx_a, mn_a);
+  group_reduce(stats_b, 0, rows_b, am_b, mx_b, mn_b);
+  if (threadIdx.x != 0) return;
+  const double qd = (double)q;
+  if (!unipolar) {
+    // abs_max = max(|max|, |min|, 1e-5); scale = abs_max / q; inv = 1 / scale
+    const double aa = fmax(fmax(fabs((double)mx_a), fabs((double)mn_a)), 1e-5);
+    const double ab = fmax(fmax(fabs((double)mx_b), fabs((double)mn_b)), 1e-5);
+    const double sa = aa / qd, sb = ab / qd;
+    scal[0] = (float)(sa * sb);
+    scal[4] = (float)(1.0 / sa);
+    scal[5] = (float)(1.0 / sb);
+    scal[1] = scal[2] = scal[3] = scal[6] = scal[7] = 0.f;
+  } else {
+    // range = max(max - min, 1e-5); scale = range / q; inv = 1 / scale;
+    // zp = clamp(round(-min / scale), 0, q)
+    const double ra = fmax((double)mx_a - (double)mn_a, 1e-5);
+    const double rb = fmax((double)mx_b - (double)mn_b, 1e-5);
+    const double sa = ra / qd, sb = rb / qd;
+    const double za = fmax(0.0, fmin(qd, rint(-(double)mn_a / sa)));
+    const double zb = fmax(0.0, fmin(qd, rint(-(double)mn_b / sb)));
+    scal[0] = (float)(sa * sb);
+    scal[1] = (float)(-zb);
+    scal[2] = (float)za;
+    scal[3] = (float)((double)d * za * zb);
+    scal[4] = (float)(1.0 / sa);
+    scal[5] = (float)(1.0 / sb);
+    scal[6] = (float)za;
+    scal[7] = (float)zb;
+  }
+}
+
+// --------------------------------------------------------------------------
+// quantisers: one warp per row
+// --------------------------------------------------------------------------
+
+template <int R>
+__global__ void quant_rows_kernel(QuantArgs q) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (row >= q.rows) return;
+  const float qf = (float)q.q;
+  int16_t* out = q.out16 + (size_t)row * q.d;
+
+  if (R == Q_ROWCHUNK_BIP) {
+    // fused_quant_kernel PER_ROW bipolar on every chunk (fused.py:65-81, 98-112)
+    const int nch = cdiv(q.d, q.chunk_d);
+    for (int c = 0; c < nch; ++c) {
+      const int j0 = c * q.chunk_d, j1 = min(j0 + q.chunk_d, q.d);
+      float am = 0.f;
+      for (int j = j0 + lane; j < j1; j += 32) am = fmaxf(am, fabsf(load_x(q, row, j)));
+      am = fmaxf(warp_max(am), 1e-5f);
+      const float sc = fdiv(am, qf);
+      const float inv = fdiv(1.0f, sc);
+      if (lane == 0) q.chunk_scale[(size_t)c * q.rows + row] = sc;
+      for (int j = j0 + lane; j < j1; j += 32) {
+        const float xc = fclamp(frint(fmul(load_x(q, row, j), inv)), -qf, qf);
+        const int bnd = (int)frint(fmul(fabsf(xc), q.ratio));
+        out[j] = encode(q, j, bnd, xc);
+      }
+    }
+    return;
+  }
+
+  float inv = 0.f, sc = 0.f, zp = 0.f;
+  if (R == Q_TENSOR_BIP || R == Q_TENSOR_UNI) {
+    inv = __ldg(q.params + q.param_off);
+    zp = R == Q_TENSOR_UNI ? __ldg(q.params + q.param_off + 2) : 0.f;
+  } else if (R == Q_HEAD_BIP) {
+    inv = __ldg(q.params + row / q.rows_per_batch);
+  } else if (q.self_stats) {
+    // G == 1: the row is its own group (grouped.py:46-47, 111-115)
+    float am = 0.f, mx = -INFINITY, mn = INFINITY;
+    for (int j = lane; j < q.d; j += 32) {
+      const float x = load_x(q, row, j);
+      am = fmaxf(am, fabsf(x));
+      mx = fmaxf(mx, x);
+      mn = fminf(mn, x);
+    }
+    am = warp_max(am);
+    mx = warp_max(mx);
+    mn = warp_min(mn);
+    if (R == Q_GROUP_ASYM) {
+      sc = fdiv(fmaxf(fsub(mx, mn), 1e-5f), qf);
+      zp = fclamp(frint(fdiv(-mn, sc)), 0.f, qf);
+    } else {
+      sc = fdiv(fmaxf(am, 1e-5f), qf);
+    }
+    if (lane == 0) {
+      q.row_scale[row] = sc;
+      if (R == Q_GROUP_ASYM) q.row_zp[row] = zp;
+    }
+  } else {
+    sc = __ldg(q.row_scale + row);
+    if (R == Q_GROUP_ASYM) zp = __ldg(q.row_zp + row);
+  }
+
+  float rsum = 0.f;
+  for (int j = lane; j < q.d; j += 32) {
+    const float x = load_x(q, row, j);
+    int bnd;
+    float sgn = 1.f;
+    if (R == Q_TENSOR_BIP || R == Q_HEAD_BIP) {
+      // fused.py:94-106 / 265-273: clamp(rint(x * inv), [qmin, q]); rint(|xc| * G/q)
+      const float xc = fclamp(frint(fmul(x, inv)), q.qmin, qf);
+      bnd = (int)frint(fmul(fabsf(xc), q.ratio));
+      sgn = xc;
+    } else if (R == Q_TENSOR_UNI) {
+      // fused.py:84, 98, 114-121: clamp(rint(x * inv + zp), 0, q)
+      const float xc = fclamp(frint(fadd(fmul(x, inv), zp)), 0.f, qf);
+      bnd = (int)frint(fmul(xc, q.ratio));
+      rsum = fadd(rsum, xc);
+    } else if (R == Q_GROUP_SYM) {
+      // grouped.py:51 + kernels.py:1679: clamp(round(x / s), +-q); round(|xi| * G / q)
+      const float xi = fclamp(frint(fdiv(x, sc)), -qf, qf);
+      bnd = (int)frint(fdiv(fmul(fabsf(xi), (float)q.G), qf));
+      sgn = xi;
+    } else if (R == Q_BATCH_SYM) {
+      // grouped.py:148/156 + kernels.py:1864: round(|xi| * fl32(G / q))
+      const float xi = fclamp(frint(fdiv(x, sc)), -qf, qf);
+      bnd = (int)frint(fmul(fabsf(xi), q.ratio));
+      sgn = xi;
+    } else {  // Q_GROUP_ASYM: grouped.py:131 + kernels.py:1685
+      const float xi = fclamp(frint(fadd(fdiv(x, sc), zp)), 0.f, qf);
+      bnd = (int)frint(fdiv(fmul(xi, (float)q.G), qf));
+      rsum = fadd(rsum, xi);
+    }
+    out[j] = encode(q, j, bnd, sgn);
+  }
+  if (q.row_sum) {
+    rsum = warp_sum(rsum);
+    if (lane == 0) q.row_sum[row] = rsum;
+  }
+}
+
+// --------------------------------------------------------------------------
+// host launchers
+// --------------------------------------------------------------------------
+
+static inline dim3 warp_grid(int rows) { return dim3(cdiv(rows, 8)); }
+
+cudaError_t launch_row_stats(const QuantArgs& q, float* stats, cudaStream_t st) {
+  if (q.rows > 0) row_stats_kernel<<<warp_grid(q.rows), 256, 0, st>>>(q, stats);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_group_params(const float* stats, int batch, int rpb, int G, int q, int recipe,
+                                float* scale, float* zp, cudaStream_t st) {
+  const int gpb = G >= rpb ? 1 : cdiv(rpb, G);
+  const int ng = recipe == GP_HEAD ? batch : batch * gpb;
+  if (ng > 0) group_params_kernel<<<ng, 256, 0, st>>>(stats, rpb, recipe == GP_HEAD ? rpb : G, q,
+                                                       recipe, scale, zp);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tensor_params(const float* sa, int ra, const float* sb, int rb, int d, int q,
+                                 int unipolar, float* scal, cudaStream_t st) {
+  tensor_params_kernel<<<1, 1024, 0, st>>>(sa, ra, sb, rb, d, q, unipolar, scal);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_rows(int recipe, const QuantArgs& q, cudaStream_t st) {
+  if (q.rows <= 0) return cudaSuccess;
+  const dim3 g = warp_grid(q.rows);
+  switch (recipe) {
+    case Q_TENSOR_BIP: quant_rows_kernel<Q_TENSOR_BIP><<<g, 256, 0, st>>>(q); break;
+    case Q_TENSOR_UNI: quant_rows_kernel<Q_TENSOR_UNI><<<g, 256, 0, st>>>(q); break;
+    case Q_GROUP_SYM: quant_rows_kernel<Q_GROUP_SYM><<<g, 256, 0, st>>>(q); break;
+    case Q_GROUP_ASYM: quant_rows_kernel<Q_GROUP_ASYM><<<g, 256, 0, st>>>(q); break;
+    case Q_BATCH_SYM: quant_rows_kernel<Q_BATCH_SYM><<<g, 256, 0, st>>>(q); break;
+    case Q_ROWCHUNK_BIP: quant_rows_kernel<Q_ROWCHUNK_BIP><<<g, 256, 0, st>>>(q); break;
+    case Q_HEAD_BIP: quant_rows_kernel<Q_HEAD_BIP><<<g, 256, 0, st>>>(q); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace scmp

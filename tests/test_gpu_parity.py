@@ -1,0 +1,169 @@
+"""Parity of the native B200 path with the reference, on the GPU.
+
+* every golden fixture (outputs of the reference's own sc_matmul) through the
+  tcgen05 path and through the CUDA-core path: bit-exact float32;
+* device tables against the reference's k_table / cum_indicator;
+* seeded random cases against the CPU oracle, bit-exact;
+* the quantiser API against the oracle's restatements.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, golden_names, load_golden
+from oracle import sc_oracle as O
+
+pytestmark = pytest.mark.gpu
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+from scmp_kernels_b200 import _lib, sc_matmul  # noqa: E402
+from scmp_kernels_b200.sc import clear_rng_cache  # noqa: E402
+from scmp_kernels_b200.sc import kernels as K  # noqa: E402
+
+DEV = "cuda:0"
+
+
+@pytest.fixture(params=["tc", "simt"])
+def impl(request, monkeypatch):
+    monkeypatch.setattr(K, "_FORCE_SIMT", request.param == "simt")
+    clear_rng_cache()
+    yield request.param
+    clear_rng_cache()
+
+
+def _run(a, b, p, s=None):
+    p = dict(p)
+    g = p.pop("granularity")
+    ta = torch.from_numpy(a).to(DEV)
+    tb = torch.from_numpy(b).to(DEV)
+    ts = torch.from_numpy(s).to(DEV) if s is not None else None
+    y = sc_matmul(ta, tb, g, smooth_scales=ts, **p)
+    assert y.device == ta.device and y.dtype == torch.float32
+    out = y.cpu().numpy()
+    assert _lib.device_error() == 0
+    return out
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_golden(name, impl, env_vars):
+    a, b, p, out, s, env = load_golden(name)
+    env_vars(env)
+    y = _run(a, b, p, s)
+    assert y.shape == out.shape
+    bad = np.argwhere(y != out)
+    assert bad.size == 0, f"{len(bad)} mismatches, first at {bad[0]}: {y[tuple(bad[0])]} vs {out[tuple(bad[0])]}"
+
+
+RNG = np.load(os.path.join(GOLDEN, "rng_golden.npz"))
+
+
+@pytest.mark.parametrize("L,G", [(256, 256), (64, 256), (64, 64), (100, 128), (256, 300), (40, 100)])
+def test_device_tables_reproduce_reference(L, G, env_vars):
+    env_vars({})
+    from scmp_kernels_b200.sc.config_helpers import make_sobol_simple_config
+    clear_rng_cache()
+    t = K._get_cached_enable_tables(make_sobol_simple_config(6, 6, 8), 8, torch.device(DEV), L, G)
+    kt = t.ktab.cpu().numpy()[t.amap.cpu().numpy()]
+    ref_k = RNG[f"ktab_L{L}_G{G}"]
+    assert np.array_equal(kt[:, :G + 1], ref_k[:, :G + 1])
+    pat = t.pattern.cpu().numpy().view(np.uint32)[t.bmap.cpu().numpy()]   # (6, vcap+1, lw)
+    bits = np.unpackbits(pat.view(np.uint8), axis=-1, bitorder="little")  # (6, vcap+1, lp)
+    cum = np.concatenate([np.zeros(bits.shape[:2] + (1,), np.int64), np.cumsum(bits, -1)], -1)
+    ref = RNG[f"cum_L{L}_G{G}"]                                           # (6, L+1, V)
+    vv = min(ref.shape[2], t.vcap + 1)
+    assert np.array_equal(cum[:, :vv, :L + 1].transpose(0, 2, 1), ref[:, :, :vv])
+
+
+CASES = [
+    dict(granularity="per_row", mode="bipolar", sc_prec=8, n=37, m=53, d=300),
+    dict(granularity="per_row", mode="unipolar", sc_prec=6, n=33, m=65, d=129, stoc_len=64),
+    dict(granularity="per_row", mode="bipolar", sc_prec=8, n=130, m=260, d=64, group_a=3, group_b=7),
+    dict(granularity="per_tensor", mode="bipolar", sc_prec=8, n=20, m=300, d=77),
+    dict(granularity="per_tensor", mode="unipolar", sc_prec=7, n=129, m=31, d=95),
+    dict(granularity="per_row", mode="bipolar", sc_prec=8, n=40, m=33, d=200, chunk_d=64, stoc_len=128,
+         rng_levels=128),
+    dict(granularity="per_row", mode="bipolar", sc_prec=8, n=17, m=29, d=150, chunk_d=72),
+    dict(granularity="per_head", mode="bipolar", sc_prec=8, bh=3, n=23, m=41, d=19),
+    dict(granularity="per_row", mode="bipolar", sc_prec=8, bh=2, n=9, m=140, d=31, stoc_len=32),
+    dict(granularity="per_row", mode="bipolar", sc_prec=5, n=140, m=270, d=48, stoc_len=20),
+]
+
+
+@pytest.mark.parametrize("case", range(len(CASES)))
+def test_random_vs_oracle(case, impl, env_vars):
+    env_vars({})
+    c = dict(CASES[case])
+    g = torch.Generator().manual_seed(1000 + case)
+    bh = c.pop("bh", None)
+    n, m, d = c.pop("n"), c.pop("m"), c.pop("d")
+    sa = (bh, n, d) if bh else (n, d)
+    sb = (bh, m, d) if bh else (m, d)
+    a = (torch.randn(*sa, generator=g) * 2).numpy()
+    b = (torch.randn(*sb, generator=g) * 0.05).numpy()
+    a.reshape(-1)[::97] = 0.0
+    y = _run(a, b, c)
+    p = dict(c)
+    gran = p.pop("granularity")
+    ref = O.sc_matmul(a, b, gran, env={}, **p)
+    assert np.array_equal(y, ref), f"max |diff| {np.abs(y - ref).max()}"
+
+
+def test_tc_matches_simt_at_size(monkeypatch, env_vars):
+    env_vars({})
+    g = torch.Generator(device=DEV).manual_seed(7)
+    a = torch.randn(300, 1000, device=DEV, generator=g)
+    b = torch.randn(520, 1000, device=DEV, generator=g) * 0.02
+    outs = []
+    for simt in (False, True):
+        monkeypatch.setattr(K, "_FORCE_SIMT", simt)
+        outs.append(sc_matmul(a, b, "per_row", sc_prec=8))
+    assert torch.equal(outs[0], outs[1])
+    assert _lib.device_error() == 0
+
+
+def test_quantiser_api_vs_oracle():
+    from scmp_kernels_b200 import quant as Q
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(37, 90, generator=g)
+    xn = x.numpy()
+    bnd, sgn, sc = Q.fused_quantize_bipolar(x.to(DEV), float(x.abs().max()), 8)
+    rb, rs, rsc = O.fused_quantize_bipolar(xn, float(x.abs().max()), 8, 256)
+    assert np.array_equal(bnd.cpu().numpy(), rb) and np.array_equal(sgn.cpu().numpy(), rs) and sc == rsc
+    bnd, sgn, scr = Q.fused_quantize_bipolar_perrow(x.to(DEV), 8, rng_levels=64)
+    rb, rs, rsc = O.fused_quantize_bipolar_perrow(xn, 8, 64)
+    assert np.array_equal(bnd.cpu().numpy(), rb) and np.array_equal(scr.cpu().numpy(), rsc)
+    bnd, sc, zp, rsum = Q.fused_quantize_unipolar(x.to(DEV), float(x.max()), float(x.min()), 6,
+                                                  compute_sum=True)
+    rb, rsc, rzp, rrs = O.fused_quantize_unipolar(xn, float(x.max()), float(x.min()), 6, 64)
+    assert np.array_equal(bnd.cpu().numpy(), rb) and sc == rsc and zp == rzp
+    assert np.array_equal(rsum.cpu().numpy(), rrs)
+    for G in (1, 4, 37, 100):
+        s, xi, sg = Q._grouped_symmetric_quant(x.to(DEV), G, 127)
+        rs_, rxi, rsg = O.grouped_symmetric_quant(xn, G, 127)
+        assert np.array_equal(s.cpu().numpy(), rs_) and np.array_equal(xi.cpu().numpy(), rxi)
+        assert np.array_equal(sg.cpu().numpy(), rsg)
+        s, zp, xi = Q._grouped_asymmetric_quant(x.to(DEV), G, 255)
+        rs_, rzp, rxi = O.grouped_asymmetric_quant(xn, G, 255)
+        assert np.array_equal(s.cpu().numpy(), rs_) and np.array_equal(zp.cpu().numpy(), rzp)
+        assert np.array_equal(xi.cpu().numpy(), rxi)
+    x3 = torch.randn(3, 11, 20, generator=g)
+    inv = (1.0 / (x3.abs().amax(dim=(1, 2)).clamp(min=1e-5) / 127)).float()
+    bnd, sgn = Q.fused_quant_bipolar_batched(x3.to(DEV), inv.to(DEV), 8)
+    rb, rs = O.fused_quant_bipolar_batched(x3.numpy(), inv.numpy(), 8, 256)
+    assert np.array_equal(bnd.cpu().numpy(), rb.transpose(0, 2, 1))
+    assert np.array_equal(sgn.cpu().numpy(), rs.transpose(0, 2, 1))
+    assert _lib.device_error() == 0
+
+
+def test_cpu_inputs_round_trip_and_device_guard():
+    a, b = torch.randn(8, 64), torch.randn(16, 64)
+    y = sc_matmul(a, b, "per_row")
+    assert y.device.type == "cpu" and y.shape == (8, 16)
+    assert torch.cuda.current_device() == 0
+    y2 = sc_matmul(a.cuda(), b.cuda(), "per_row")
+    assert torch.equal(y, y2.cpu())
