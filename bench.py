@@ -47,20 +47,24 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shape", default=None,
+                    help="N,M,D override of the config2/config5 recipes (smaller cases for profiling)")
     return ap.parse_args()
 
 
-def build_workload(name, device):
+def build_workload(name, device, shape=None):
     """Returns (a, b, kwargs, bh_n_m_d, L, label, calls) with calls = list of
     (a_rows_index or None, kwargs) for workloads composed of several calls."""
     from scmp_kernels_b200 import workloads as W
     if name == "config2":
-        a, b = W.config2(device)
-        return a, b, None, dict(granularity="per_row", mode="bipolar", sc_prec=8), (1, 4096, 11008, 4096), 256
+        n, m, d = shape or (4096, 11008, 4096)
+        a, b = W.config2(device, n, m, d)
+        return a, b, None, dict(granularity="per_row", mode="bipolar", sc_prec=8), (1, n, m, d), 256
     if name == "config5":
-        a, b, s = W.config5(device)
+        n, m, d = shape or (8192, 28672, 8192)
+        a, b, s = W.config5(device, n, m, d)
         return a, b, s, dict(granularity="per_row", mode="unipolar", sc_prec=6, stoc_len=64), \
-            (1, 8192, 28672, 8192), 64
+            (1, n, m, d), 64
     if name in ("config3qk", "config3av"):
         q, k, probs, v_t = W.config3(device)
         if name == "config3qk":
@@ -194,7 +198,8 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
-    a, b, s, kw, (BH, N, M, D), L = build_workload(args.workload, dev)
+    shape = tuple(int(x) for x in args.shape.split(",")) if args.shape else None
+    a, b, s, kw, (BH, N, M, D), L = build_workload(args.workload, dev, shape)
     # shard the weight operand by rows
     if world > 1:
         rows = b.shape[-2]
