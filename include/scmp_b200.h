@@ -117,6 +117,21 @@ int scmp_sc_matmul(const scmp_matmul_desc* desc, void* workspace, size_t workspa
                    void* stream);
 
 /*
+ * scmp_sc_matmul without a caller workspace. No counterpart in the reference.
+ * For callers that cannot allocate device memory (a host reaching this
+ * library through a plain C FFI with no device allocator, or a process that
+ * reserved all its device memory up front and must not call cudaMalloc,
+ * which can also synchronise the device). Runs the same pipeline on a fixed
+ * 16 MiB scratch array inside the library's device image (present on every
+ * GPU that loads the library until exit); allocates and frees nothing. The
+ * first call on a device looks up that array's address, so make it before
+ * any stream capture. Calls needing more than 16 MiB of scratch (see
+ * scmp_sc_matmul_workspace_size) return SCMP_ERR_INVALID_ARG. All calls on a
+ * device share the array: calls that overlap on the GPU race.
+ */
+int scmp_sc_matmul_noalloc(const scmp_matmul_desc* desc, void* stream);
+
+/*
  * Enable-signal matmul on already-quantised operands.
  * Replaces enable_matmul_triton + enable_matmul_tiled_kernel
  * (scmp_kernels/sc/kernels.py:798-868, 176-252).

@@ -52,6 +52,7 @@ SIGNATURES = {
                                   c_void_p, c_void_p]),
     "scmp_sc_matmul_workspace_size": (c_int, [ctypes.POINTER(MatmulDesc), ctypes.POINTER(c_size_t)]),
     "scmp_sc_matmul": (c_int, [ctypes.POINTER(MatmulDesc), c_void_p, c_size_t, c_void_p]),
+    "scmp_sc_matmul_noalloc": (c_int, [ctypes.POINTER(MatmulDesc), c_void_p]),
     "scmp_enable_matmul_workspace_size": (c_int, [c_int, c_int, c_int, ctypes.POINTER(c_size_t)]),
     "scmp_enable_matmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                    c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,

@@ -6,3 +6,4 @@
 #include "gemm_tc.cu"
 #include "api.cu"
 #include "quant_ref.cu"
+#include "noalloc.cu"
