@@ -41,7 +41,7 @@ WORKLOADS = {
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="config2", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -231,6 +231,7 @@ def main():
             return out_full
         return y
 
+    clk_p, clk_f = clocks_start(local)  # sampled from warm-up to the end of the timed steps
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -243,7 +244,6 @@ def main():
         e0.record()
         e1.record()
     torch.cuda.synchronize()
-    clk_p, clk_f = clocks_start(local)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()

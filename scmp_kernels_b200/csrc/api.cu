@@ -10,6 +10,17 @@ namespace scmp {
 static thread_local std::string t_last_error;
 static cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
 
+// Copy of the dimension -> table-row map padded with zeros to 8*ceil(d/8),
+// so the GEMM can read it in aligned blocks of eight.
+__global__ void pad_map_kernel(const int32_t* __restrict__ src, int d, int32_t* __restrict__ dst) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < d8(d) * 8) dst[i] = i < d ? src[i] : 0;
+}
+static cudaError_t launch_pad_map(const int32_t* src, int d, int32_t* dst, cudaStream_t st) {
+  pad_map_kernel<<<cdiv(d8(d) * 8, 256), 256, 0, st>>>(src, d, dst);
+  return cudaGetLastError();
+}
+
 // SC-GEMM launch bracketed by the optional profiling events.
 static cudaError_t launch_gemm(const GemmArgs& g, int flags, cudaStream_t st) {
   if (g_prof_start) cudaEventRecord(g_prof_start, st);
@@ -48,6 +59,7 @@ struct Carver {
 struct Plan {
   int16_t* ka = nullptr;
   int16_t* vb = nullptr;
+  int32_t* bmap = nullptr;
   float* stats_a = nullptr;
   float* stats_b = nullptr;
   float* scale_a = nullptr;
@@ -98,8 +110,10 @@ static bool is_chunked(const scmp_matmul_desc* d) {
 
 static void carve(const scmp_matmul_desc* d, Carver& c, Plan& p) {
   const size_t na = (size_t)d->batch * d->n, nb = (size_t)d->batch * d->m;
-  p.ka = c.take<int16_t>(na * d->d);
-  p.vb = c.take<int16_t>(nb * d->d);
+  const size_t dd = (size_t)d8(d->d) * 8;
+  p.ka = c.take<int16_t>(na * dd);
+  p.vb = c.take<int16_t>(nb * dd);
+  p.bmap = c.take<int32_t>(dd);
   p.chunked = is_chunked(d);
   p.nchunks = p.chunked ? cdiv(d->d, d->chunk_d) : 1;
   const size_t rows_a = p.chunked ? na * p.nchunks : na, rows_b = p.chunked ? nb * p.nchunks : nb;
@@ -219,7 +233,8 @@ int scmp_sc_matmul(const scmp_matmul_desc* d, void* workspace, size_t workspace_
   g.ka = p.ka;
   g.vb = p.vb;
   g.pattern = d->pattern;
-  g.bmap = d->bmap;
+  g.bmap = p.bmap;
+  SCMP_CUDA(launch_pad_map(d->bmap, d->d, p.bmap, st), "pad bmap");
   g.unit_d = d->d;
   g.out = d->out;
   g.epi.inner = (float)(q * q) / (float)d->stoc_len;

@@ -27,8 +27,7 @@ __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(GemmArgs g) {
   const int ty = tid / 16, tx = tid % 16;
   const int bh = blockIdx.z;
   const int a0 = blockIdx.y * TA, b0 = blockIdx.x * TB;
-  const int16_t* ka = g.ka + (size_t)bh * g.n * g.d;
-  const int16_t* vb = g.vb + (size_t)bh * g.m * g.d;
+  const int Ra = g.batch * g.n, Rb = g.batch * g.m;  // rows of the blocked operands
 
   float run[4][4];
   int S[4][4];
@@ -52,14 +51,14 @@ __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(GemmArgs g) {
       for (int e = tid; e < DB * TA; e += THREADS) {
         const int dl = e / TA, r = e % TA, d = dd + dl;
         int16_t v = 0;
-        if (d < d1 && a0 + r < g.n) v = ka[(size_t)(a0 + r) * g.d + d];
+        if (d < d1 && a0 + r < g.n) v = g.ka[blk_idx(Ra, bh * g.n + a0 + r, d)];
         sk[dl * TA + r] = v;
       }
       // stage b: stream words and their prefix popcounts
       {
         const int dl = tid / TB, r = tid % TB, d = dd + dl;
         int vv = 0;
-        if (d < d1 && b0 + r < g.m) vv = vb[(size_t)(b0 + r) * g.d + d];
+        if (d < d1 && b0 + r < g.m) vv = g.vb[blk_idx(Rb, bh * g.m + b0 + r, d)];
         const int v = vv < 0 ? -vv : vv;
         uint32_t* w = pw + (dl * TB + r) * lw1;
         uint32_t* p = pre + (dl * TB + r) * lw1;

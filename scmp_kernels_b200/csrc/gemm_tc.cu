@@ -81,25 +81,21 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
-#define TMEM_LD32(taddr, r)                                                                        \
+#define TMEM_LD16(taddr, r)                                                                        \
   asm volatile(                                                                                    \
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14," \
-      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"               \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14," \
+      "%15}, [%16];"                                                                               \
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),       \
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),   \
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),             \
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),             \
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])              \
+        "=r"(r[14]), "=r"(r[15])                                                                   \
       : "r"(taddr))
-#define TMEM_ST32(taddr, r)                                                                        \
+#define TMEM_ST16(taddr, r)                                                                        \
   asm volatile(                                                                                    \
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13," \
-      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr), \
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13," \
+      "%14,%15,%16};" ::"r"(taddr),                                                                \
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),     \
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),           \
-      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),         \
-      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),         \
-      "r"(r[29]), "r"(r[30]), "r"(r[31]))
+      "r"(r[15]))
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -123,6 +119,60 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& g, const Sched& s, i
   b0 = (r % s.tiles_b) * BN;
 }
 
+template <int TLEN, int SPD>
+__host__ __device__ constexpr int SPB() {  // stages per block of eight dimensions
+  return (TLEN < 256 ? 8 / (256 / TLEN) : 8) * SPD;
+}
+
+// Signed value of dimension e (0..7, compile-time after unrolling) of a block.
+__device__ __forceinline__ int kv_at(const uint4& v, int e) {
+  const uint32_t w = e < 2 ? v.x : e < 4 ? v.y : e < 6 ? v.z : v.w;
+  return (int)(int16_t)((e & 1) ? (w >> 16) : (w & 0xFFFFu));
+}
+__device__ __forceinline__ int bm_at(const int4& lo, const int4& hi, int e) {
+  return e == 0 ? lo.x : e == 1 ? lo.y : e == 2 ? lo.z : e == 3 ? lo.w
+       : e == 4 ? hi.x : e == 5 ? hi.y : e == 6 ? hi.z : hi.w;
+}
+
+// The 8 stream words (256 bits) that stage j of a block expands: for each of
+// its DPS dimensions, TLEN bits of the row (bmap, |v|), starting at bit
+// (j % SPD) * TLEN. Dimensions past d1, empty rows and v == 0 give zeros.
+template <int TLEN, int SPD>
+__device__ __forceinline__ void load_stream_words(const GemmArgs& g, const uint4& kv, const int4& bl,
+                                                  const int4& bh, int j, int dbase, int d1, bool valid,
+                                                  uint32_t LW, uint32_t (&pw)[8]) {
+  constexpr int DPS = TLEN < 256 ? 256 / TLEN : 1;
+  constexpr int NW = TLEN / 32;
+#pragma unroll
+  for (int dl = 0; dl < DPS; ++dl) {
+    const int e = (j / SPD) * DPS + dl;
+    const int v = kv_at(kv, e);
+    const int mag = v < 0 ? -v : v;
+    if (valid && dbase + e < d1 && mag != 0) {
+      const uint32_t* p = g.pattern + ((size_t)bm_at(bl, bh, e) * (g.vcap + 1) + mag) * LW +
+                          (j % SPD) * NW;
+      if constexpr (NW == 8) {
+        const uint4 x = __ldg(reinterpret_cast<const uint4*>(p));
+        const uint4 y = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+        pw[0] = x.x; pw[1] = x.y; pw[2] = x.z; pw[3] = x.w;
+        pw[4] = y.x; pw[5] = y.y; pw[6] = y.z; pw[7] = y.w;
+      } else if constexpr (NW == 4) {
+        const uint4 x = __ldg(reinterpret_cast<const uint4*>(p));
+        pw[dl * 4 + 0] = x.x; pw[dl * 4 + 1] = x.y; pw[dl * 4 + 2] = x.z; pw[dl * 4 + 3] = x.w;
+      } else if constexpr (NW == 2) {
+        const uint2 x = __ldg(reinterpret_cast<const uint2*>(p));
+        pw[dl * 2] = x.x;
+        pw[dl * 2 + 1] = x.y;
+      } else {
+        pw[dl] = __ldg(p);
+      }
+    } else {
+#pragma unroll
+      for (int x = 0; x < NW; ++x) pw[dl * NW + x] = 0u;
+    }
+  }
+}
+
 template <int TLEN>
 __device__ __forceinline__ int stages_of_unit(int len) {
   if (TLEN < 256) return cdiv(len, 256 / TLEN);
@@ -131,9 +181,9 @@ __device__ __forceinline__ int stages_of_unit(int len) {
 
 // TLEN: padded stream length lp when lp <= 256 (256/lp dimensions per stage),
 // or 256*k for lp = 256*k (k stages per dimension); here TLEN = min(lp, 256)
-// and SPD = lp / TLEN stages per dimension.
-template <int TLEN>
-__global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched sc, int spd) {
+// and SPD = lp / TLEN stages per dimension (1 or 2).
+template <int TLEN, int SPD>
+__global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched sc) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sbase = (raw + 1023u) & ~1023u;          // SW128 tiles need 1024-B alignment
@@ -176,70 +226,107 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched s
 
   if (warp < PROD_A_WARPS + PROD_B_WARPS) {
     // ------------------------------------------------------------ producers
+    // Operands arrive in blocks of eight dimensions: one 16-byte load per
+    // thread (its row's signed k or v values, blocked layout) and, for b, two
+    // 16-byte loads of the block's table rows. Blocks are fetched one block
+    // ahead and b's stream words one stage ahead, so the loads are in flight
+    // while the producer waits for its shared-memory slot.
     const bool side_a = warp < PROD_A_WARPS;
     const int r = side_a ? threadIdx.x : threadIdx.x - PROD_A_WARPS * 32;
+    const int R = side_a ? g.batch * g.n : g.batch * g.m;
+    const uint4* kvsrc = reinterpret_cast<const uint4*>(side_a ? g.ka : g.vb);
+    const int4* bmsrc = reinterpret_cast<const int4*>(g.bmap);
+    const uint32_t LW = (uint32_t)g.lp / 32;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < sc.tiles; tile += gridDim.x) {
       int bh, a0, b0;
       tile_coords(g, sc, tile, bh, a0, b0);
       const int row = side_a ? a0 + r : b0 + r;
       const bool valid = side_a ? row < g.n : row < g.m;
-      const int16_t* src = side_a ? g.ka + ((size_t)bh * g.n + (valid ? row : 0)) * g.d
-                                  : g.vb + ((size_t)bh * g.m + (valid ? row : 0)) * g.d;
+      const int grow = bh * (side_a ? g.n : g.m) + (valid ? row : 0);
       for (int u = 0; u < sc.nunits; ++u) {
         const int d0 = u * sc.unit_d, d1 = min(d0 + sc.unit_d, g.d);
-        const int nst = stages_of_unit<TLEN>(d1 - d0) * spd;
-        for (int st = 0; st < nst; ++st, ++it) {
-          const int s = it % NST;
-          if (!mbar_wait(empty_bar(s), ((it / NST) & 1) ^ 1, abort_flag, side_a ? 1 : 2)) goto done;
-          const uint32_t stage = sbase + s * STAGE_BYTES;
-          const int dfirst = d0 + (st / spd) * DPS;
-          const int tbase = (st % spd) * TLEN;
-#pragma unroll
-          for (int dl = 0; dl < DPS; ++dl) {
-            const int d = dfirst + dl;
-            const int kv = (valid && d < d1) ? (int)__ldg(src + d) : 0;
-            const int mag = kv < 0 ? -kv : kv;
-            if (side_a) {
-              const uint32_t fill = kv < 0 ? 0xFFFFFFFFu : 0x01010101u;
-#pragma unroll
-              for (int c = 0; c < TLEN / 16; ++c) {
-                const int r8 = 8 * (mag - tbase - 16 * c);
-                uint32_t w[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  const int sh = max(r8 - 32 * j, 0);
-                  w[j] = fill & __funnelshift_lc(0xFFFFFFFFu, 0u, (uint32_t)sh);
-                }
-                st_shared_v4(swz(stage, A_ATOM, r, dl * (TLEN / 16) + c), w[0], w[1], w[2], w[3]);
-              }
-            } else {
-              const uint32_t mult = kv < 0 ? 0xFFu : 1u;
-              uint32_t pw[TLEN / 32];
-              if (valid && d < d1 && mag != 0) {
-                const uint32_t* p = g.pattern +
-                                    ((size_t)__ldg(g.bmap + d) * (g.vcap + 1) + mag) * (g.lp / 32) + tbase / 32;
-#pragma unroll
-                for (int x = 0; x < TLEN / 32; ++x) pw[x] = __ldg(p + x);
-              } else {
-#pragma unroll
-                for (int x = 0; x < TLEN / 32; ++x) pw[x] = 0u;
-              }
-#pragma unroll
-              for (int c = 0; c < TLEN / 16; ++c) {
-                const uint32_t bits = (pw[c >> 1] >> (16 * (c & 1))) & 0xFFFFu;
-                uint32_t w[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  const uint32_t nib = (bits >> (4 * j)) & 0xFu;
-                  w[j] = ((nib * 0x00204081u) & 0x01010101u) * mult;
-                }
-                st_shared_v4(swz(stage + A_BYTES, B_ATOM, r, dl * (TLEN / 16) + c), w[0], w[1], w[2], w[3]);
-              }
+        const int nst = stages_of_unit<TLEN>(d1 - d0) * SPD;
+        const int nblk = cdiv(d1 - d0, 8);
+        const int blk0 = d0 >> 3;
+        uint4 kv_cur = valid ? __ldg(kvsrc + (size_t)blk0 * R + grow) : make_uint4(0, 0, 0, 0);
+        int4 bm_lo = make_int4(0, 0, 0, 0), bm_hi = make_int4(0, 0, 0, 0);
+        if (!side_a) {
+          bm_lo = __ldg(bmsrc + 2 * blk0);
+          bm_hi = __ldg(bmsrc + 2 * blk0 + 1);
+        }
+        uint32_t pw[8];
+        if (!side_a) load_stream_words<TLEN, SPD>(g, kv_cur, bm_lo, bm_hi, 0, d0, d1, valid, LW, pw);
+        for (int blk = 0; blk < nblk; ++blk) {
+          const int dbase = d0 + 8 * blk;
+          const bool more = blk + 1 < nblk;
+          uint4 kv_nxt = make_uint4(0, 0, 0, 0);
+          int4 nb_lo = make_int4(0, 0, 0, 0), nb_hi = make_int4(0, 0, 0, 0);
+          if (more) {
+            if (valid) kv_nxt = __ldg(kvsrc + (size_t)(blk0 + blk + 1) * R + grow);
+            if (!side_a) {
+              nb_lo = __ldg(bmsrc + 2 * (blk0 + blk + 1));
+              nb_hi = __ldg(bmsrc + 2 * (blk0 + blk + 1) + 1);
             }
           }
-          fence_proxy_async();
-          mbar_arrive(full_bar(s));
+#pragma unroll
+          for (int j = 0; j < SPB<TLEN, SPD>(); ++j) {
+            if (blk * SPB<TLEN, SPD>() + j >= nst) break;
+            uint32_t pn[8];
+            if (!side_a) {
+              if (j + 1 < SPB<TLEN, SPD>())
+                load_stream_words<TLEN, SPD>(g, kv_cur, bm_lo, bm_hi, j + 1, dbase, d1, valid, LW, pn);
+              else
+                load_stream_words<TLEN, SPD>(g, kv_nxt, nb_lo, nb_hi, 0, dbase + 8, more ? d1 : dbase, valid, LW, pn);
+            }
+            const int s = it % NST;
+            if (!mbar_wait(empty_bar(s), ((it / NST) & 1) ^ 1, abort_flag, side_a ? 1 : 2)) goto done;
+            const uint32_t stage = sbase + s * STAGE_BYTES;
+            const int tbase = (j % SPD) * TLEN;
+#pragma unroll
+            for (int dl = 0; dl < DPS; ++dl) {
+              const int e = (j / SPD) * DPS + dl;  // dimension inside the block
+              const int kv = (dbase + e < d1) ? kv_at(kv_cur, e) : 0;
+              const int mag = kv < 0 ? -kv : kv;
+              if (side_a) {
+                const uint32_t fill = kv < 0 ? 0xFFFFFFFFu : 0x01010101u;
+#pragma unroll
+                for (int c = 0; c < TLEN / 16; ++c) {
+                  const int r8 = 8 * (mag - tbase - 16 * c);
+                  uint32_t w[4];
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    const int sh = max(r8 - 32 * q, 0);
+                    w[q] = fill & __funnelshift_lc(0xFFFFFFFFu, 0u, (uint32_t)sh);
+                  }
+                  st_shared_v4(swz(stage, A_ATOM, r, dl * (TLEN / 16) + c), w[0], w[1], w[2], w[3]);
+                }
+              } else {
+                const uint32_t mult = kv < 0 ? 0xFFu : 1u;
+#pragma unroll
+                for (int c = 0; c < TLEN / 16; ++c) {
+                  const uint32_t bits = (pw[dl * (TLEN / 32) + (c >> 1)] >> (16 * (c & 1))) & 0xFFFFu;
+                  uint32_t w[4];
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    const uint32_t nib = (bits >> (4 * q)) & 0xFu;
+                    w[q] = ((nib * 0x00204081u) & 0x01010101u) * mult;
+                  }
+                  st_shared_v4(swz(stage + A_BYTES, B_ATOM, r, dl * (TLEN / 16) + c), w[0], w[1], w[2], w[3]);
+                }
+              }
+            }
+            fence_proxy_async();
+            mbar_arrive(full_bar(s));
+            ++it;
+            if (!side_a) {
+#pragma unroll
+              for (int x = 0; x < 8; ++x) pw[x] = pn[x];
+            }
+          }
+          kv_cur = kv_nxt;
+          bm_lo = nb_lo;
+          bm_hi = nb_hi;
         }
       }
     }
@@ -252,7 +339,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched s
           if (!mbar_wait(acce_bar, (uc & 1) ^ 1, abort_flag, 4)) goto mma_done;
           tc_fence_after();
           const int d0 = u * sc.unit_d, d1 = min(d0 + sc.unit_d, g.d);
-          const int nst = stages_of_unit<TLEN>(d1 - d0) * spd;
+          const int nst = stages_of_unit<TLEN>(d1 - d0) * SPD;
           for (int st = 0; st < nst; ++st, ++it) {
             const int s = it % NST;
             if (!mbar_wait(full_bar(s), (it / NST) & 1, abort_flag, 3)) goto mma_done;
@@ -294,14 +381,14 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched s
         tc_fence_after();
         const bool last = u == sc.nunits - 1;
 #pragma unroll 1
-        for (int cb = 0; cb < BN / 32; ++cb) {
-          uint32_t acc[32], run[32];
-          TMEM_LD32(lane_addr + cb * 32, acc);
-          if (chunked && u > 0) TMEM_LD32(lane_addr + 256 + cb * 32, run);
+        for (int cb = 0; cb < BN / 16; ++cb) {
+          uint32_t acc[16], run[16];
+          TMEM_LD16(lane_addr + cb * 16, acc);
+          if (chunked && u > 0) TMEM_LD16(lane_addr + 256 + cb * 16, run);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int ib = b0 + cb * 32 + j;
+          for (int j = 0; j < 16; ++j) {
+            const int ib = b0 + cb * 16 + j;
             float v = 0.f;
             if (ia < g.n && ib < g.m)
               v = epi_value(g.epi, (int)acc[j], bh * g.n + ia, bh * g.m + ib, bh, u, g.n, g.m);
@@ -312,13 +399,13 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched s
             if (ia < g.n) {
               float* o = g.out + ((size_t)bh * g.n + ia) * g.m;
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int ib = b0 + cb * 32 + j;
+              for (int j = 0; j < 16; ++j) {
+                const int ib = b0 + cb * 16 + j;
                 if (ib < g.m) o[ib] = __uint_as_float(run[j]);
               }
             }
           } else {
-            TMEM_ST32(lane_addr + 256 + cb * 32, run);
+            TMEM_ST16(lane_addr + 256 + cb * 16, run);
           }
         }
         if (chunked && !last) tmem_wait_st();
@@ -337,16 +424,16 @@ done:
   }
 }
 
-template <int TLEN>
-static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int spd, int grid, cudaStream_t st) {
+template <int TLEN, int SPD>
+static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int grid, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
     cudaError_t e =
-        cudaFuncSetAttribute(gemm_tc_kernel<TLEN>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaFuncSetAttribute(gemm_tc_kernel<TLEN, SPD>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  gemm_tc_kernel<TLEN><<<grid, THREADS, SMEM_BYTES, st>>>(g, s, spd);
+  gemm_tc_kernel<TLEN, SPD><<<grid, THREADS, SMEM_BYTES, st>>>(g, s);
   return cudaGetLastError();
 }
 
@@ -354,8 +441,10 @@ static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int spd, int grid
 
 bool gemm_tc_supported(const GemmArgs& g) {
   if (g.n <= 0 || g.m <= 0 || g.d <= 0) return false;
-  if (g.lp < 32 || (g.lp & (g.lp - 1))) return false;  // power of two >= 32
+  if (g.lp < 32 || g.lp > 512 || (g.lp & (g.lp - 1))) return false;  // power of two in [32, 512]
   if ((long long)g.d * g.L >= (1LL << 31)) return false;
+  // accumulation units (chunks) must start on a block of eight dimensions
+  if (g.unit_d > 0 && g.unit_d < g.d && g.unit_d % 8 != 0) return false;
   int dev = 0, major = 0, minor = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
@@ -378,10 +467,10 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
   const int tlen = g.lp < 256 ? g.lp : 256;
   const int spd = g.lp / tlen;
   switch (tlen) {
-    case 32: return launch_t<32>(g, s, spd, grid, st);
-    case 64: return launch_t<64>(g, s, spd, grid, st);
-    case 128: return launch_t<128>(g, s, spd, grid, st);
-    default: return launch_t<256>(g, s, spd, grid, st);
+    case 32: return launch_t<32, 1>(g, s, grid, st);
+    case 64: return launch_t<64, 1>(g, s, grid, st);
+    case 128: return launch_t<128, 1>(g, s, grid, st);
+    default: return spd == 2 ? launch_t<256, 2>(g, s, grid, st) : launch_t<256, 1>(g, s, grid, st);
   }
 }
 

@@ -65,9 +65,19 @@ __device__ __forceinline__ float epi_value(const Epilogue& e, int S, int ia, int
   }
 }
 
+// Operand layout of the quantised operands: int16 [ceil(d/8)][R][8] with
+// R = batch * rows, so that one aligned 16-byte load gives a thread eight
+// consecutive dimensions of its row and a warp's 32 consecutive rows are one
+// contiguous 512-byte segment. Entries past d are padding (never read as data).
+__host__ __device__ __forceinline__ int d8(int d) { return (d + 7) >> 3; }
+__host__ __device__ __forceinline__ size_t blk_idx(int R, int row, int j) {
+  return ((size_t)(j >> 3) * R + row) * 8 + (j & 7);
+}
+
 // SC-GEMM operands and epilogue.
-//   ka: (batch, n, d) int16, signed thermometer length sa * k of operand a;
-//   vb: (batch, m, d) int16, signed boundary sb * v of operand b;
+//   ka: signed thermometer length sa * k of operand a, blocked (R = batch*n);
+//   vb: signed boundary sb * v of operand b, blocked (R = batch*m);
+//   bmap: table row of every dimension, padded with zeros to 8*ceil(d/8);
 //   pattern/bmap: comparator streams of b, bit t of row (bmap[j], v);
 //   the d range is split into accumulation units of unit_d dimensions (the
 //   chunks of the chunked path; one unit of d otherwise).

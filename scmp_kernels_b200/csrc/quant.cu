@@ -189,7 +189,7 @@ __global__ void quant_rows_kernel(QuantArgs q) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (row >= q.rows) return;
   const float qf = (float)q.q;
-  int16_t* out = q.out16 + (size_t)row * q.d;
+  int16_t* out = q.out16;  // blocked [d/8][rows][8] layout (blk_idx)
 
   if (R == Q_ROWCHUNK_BIP) {
     // fused_quant_kernel PER_ROW bipolar on every chunk (fused.py:65-81, 98-112)
@@ -205,7 +205,7 @@ __global__ void quant_rows_kernel(QuantArgs q) {
       for (int j = j0 + lane; j < j1; j += 32) {
         const float xc = fclamp(frint(fmul(load_x(q, row, j), inv)), -qf, qf);
         const int bnd = (int)frint(fmul(fabsf(xc), q.ratio));
-        out[j] = encode(q, j, bnd, xc);
+        out[blk_idx(q.rows, row, j)] = encode(q, j, bnd, xc);
       }
     }
     return;
@@ -274,7 +274,7 @@ __global__ void quant_rows_kernel(QuantArgs q) {
       bnd = (int)frint(fdiv(fmul(xi, (float)q.G), qf));
       rsum = fadd(rsum, xi);
     }
-    out[j] = encode(q, j, bnd, sgn);
+    out[blk_idx(q.rows, row, j)] = encode(q, j, bnd, sgn);
   }
   if (q.row_sum) {
     rsum = warp_sum(rsum);

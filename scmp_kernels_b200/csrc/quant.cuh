@@ -35,7 +35,7 @@ struct QuantArgs {
   int chunk_d;          // Q_ROWCHUNK_BIP
   float* chunk_scale;   // (nchunks, rows)
   // outputs
-  int16_t* out16;       // (rows, d)
+  int16_t* out16;       // blocked [ceil(d/8)][rows][8] (internal.cuh: blk_idx)
   const int16_t* ktab;  // non-NULL for operand a: map boundary -> k
   const int32_t* amap;
   int vcap;

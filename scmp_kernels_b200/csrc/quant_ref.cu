@@ -81,18 +81,20 @@ __global__ void ref_grouped_kernel(const float* __restrict__ x, size_t total, in
   }
 }
 
-// Reference-format (boundary, sign) -> signed thermometer length / boundary.
+// Reference-format (boundary, sign) -> signed thermometer length / boundary,
+// written in the GEMM's blocked layout.
 __global__ void encode_kernel(const int16_t* __restrict__ bnd, const int8_t* __restrict__ sgn,
-                              size_t total, int d, const int16_t* __restrict__ ktab,
+                              size_t total, int rows, int d, const int16_t* __restrict__ ktab,
                               const int32_t* __restrict__ map, int vcap,
                               int16_t* __restrict__ out) {
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
   const int j = (int)(i % d);
+  const int row = (int)(i / d);
   int v = bnd[i];
   v = v < 0 ? 0 : (v < vcap ? v : vcap);
   if (ktab) v = ktab[(size_t)map[j] * (vcap + 1) + v];
-  out[i] = (int16_t)(sgn && sgn[i] < 0 ? -v : v);
+  out[blk_idx(rows, row, j)] = (int16_t)(sgn && sgn[i] < 0 ? -v : v);
 }
 
 }  // namespace scmp
@@ -210,10 +212,21 @@ int scmp_grouped_asymmetric_quant(const float* x, int rows, int cols, int group,
   return e == cudaSuccess ? SCMP_OK : scmp::fail(SCMP_ERR_CUDA, cudaGetErrorString(e));
 }
 
+static void carve_enable(int n, int m, int d, scmp::Carver& c, int16_t** ka, int16_t** vb,
+                         int32_t** bmap) {
+  const size_t dd = (size_t)scmp::d8(d) * 8;
+  *ka = c.take<int16_t>((size_t)n * dd);
+  *vb = c.take<int16_t>((size_t)m * dd);
+  *bmap = c.take<int32_t>(dd);
+}
+
 int scmp_enable_matmul_workspace_size(int n, int m, int d, size_t* bytes) {
   if (n < 0 || m < 0 || d < 1 || !bytes) return scmp::fail(SCMP_ERR_INVALID_ARG, "enable_matmul_workspace_size: bad arguments");
-  const size_t a = (((size_t)n * d * 2) + 255) & ~size_t(255);
-  *bytes = a + (size_t)m * d * 2;
+  scmp::Carver c;
+  int16_t *ka, *vb;
+  int32_t* bm;
+  carve_enable(n, m, d, c, &ka, &vb, &bm);
+  *bytes = c.off;
   return SCMP_OK;
 }
 
@@ -228,11 +241,15 @@ int scmp_enable_matmul(const int16_t* ktab, const uint32_t* pattern, const int32
   if (n == 0 || m == 0) return SCMP_OK;
   if (!workspace || workspace_bytes < need) return scmp::fail(SCMP_ERR_WORKSPACE, "enable_matmul: workspace missing or too small");
   cudaStream_t st = (cudaStream_t)stream;
-  int16_t* ka = static_cast<int16_t*>(workspace);
-  int16_t* vb = reinterpret_cast<int16_t*>(static_cast<char*>(workspace) + ((((size_t)n * d * 2) + 255) & ~size_t(255)));
+  scmp::Carver c{static_cast<char*>(workspace), 0};
+  int16_t *ka, *vb;
+  int32_t* bm;
+  carve_enable(n, m, d, c, &ka, &vb, &bm);
   const size_t ta = (size_t)n * d, tb = (size_t)m * d;
-  encode_kernel<<<(unsigned)((ta + 255) / 256), 256, 0, st>>>(boundary_a, is_bipolar ? sign_a : nullptr, ta, d, ktab, amap, vcap, ka);
-  encode_kernel<<<(unsigned)((tb + 255) / 256), 256, 0, st>>>(boundary_b, is_bipolar ? sign_b : nullptr, tb, d, nullptr, bmap, vcap, vb);
+  encode_kernel<<<(unsigned)((ta + 255) / 256), 256, 0, st>>>(boundary_a, is_bipolar ? sign_a : nullptr, ta, n, d, ktab, amap, vcap, ka);
+  encode_kernel<<<(unsigned)((tb + 255) / 256), 256, 0, st>>>(boundary_b, is_bipolar ? sign_b : nullptr, tb, m, d, nullptr, bmap, vcap, vb);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = scmp::launch_pad_map(bmap, d, bm, st);
   GemmArgs g{};
   g.batch = 1;
   g.n = n;
@@ -245,12 +262,11 @@ int scmp_enable_matmul(const int16_t* ktab, const uint32_t* pattern, const int32
   g.ka = ka;
   g.vb = vb;
   g.pattern = pattern;
-  g.bmap = bmap;
+  g.bmap = bm;
   g.unit_d = d;
   g.out = out;
   g.epi.kind = EPI_RAW;
   g.epi.inner = q_max_sq / (float)L;
-  cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) e = scmp::launch_gemm(g, flags, st);
   return e == cudaSuccess ? SCMP_OK : scmp::fail(SCMP_ERR_CUDA, cudaGetErrorString(e));
 }
