@@ -135,20 +135,20 @@ def cpu_baseline(workload, max_seconds=20.0):
         have_c = False
     g = torch.Generator().manual_seed(0)
     if workload == "config5":
-        a, b = W.outlier_activations(64, 8192, g, "cpu"), torch.randn(64, 8192, generator=g) * 0.015
+        a, b = W.outlier_activations(1024, 8192, g, "cpu"), torch.randn(1024, 8192, generator=g) * 0.015
         p, L, D = dict(granularity="per_row", mode="unipolar", sc_prec=6, stoc_len=64), 64, 8192
     elif workload.startswith("config3"):
-        a, b = torch.randn(2, 197, 64, generator=g), torch.randn(2, 197, 64, generator=g)
+        a, b = torch.randn(16, 197, 64, generator=g), torch.randn(16, 197, 64, generator=g)
         p, L, D = dict(granularity="per_head", sc_prec=8), 256, 64
     else:
-        a, b = W.outlier_activations(64, 4096, g, "cpu"), torch.randn(64, 4096, generator=g) * 0.02
+        a, b = W.outlier_activations(1024, 4096, g, "cpu"), torch.randn(1024, 4096, generator=g) * 0.02
         p, L, D = dict(granularity="per_row", mode="bipolar", sc_prec=8), 256, 4096
     an, bn = a.numpy(), b.numpy()
     q = dict(p)
     gran = q.pop("granularity")
     rows = 8
     while True:
-        sa, sb = an[..., :rows, :], bn[..., :rows, :]
+        sa, sb = np.ascontiguousarray(an[..., :rows, :]), np.ascontiguousarray(bn[..., :rows, :])
         t0 = time.perf_counter()
         if have_c:
             CO.sc_matmul(sa, sb, gran, threads=threads, **q)

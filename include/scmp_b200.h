@@ -108,6 +108,11 @@ typedef struct scmp_matmul_desc {
   int vcap;                /* as passed to scmp_build_tables                       */
   int lp;                  /* as passed to scmp_build_tables                       */
   int flags;               /* SCMP_FLAG_*                                          */
+  const double* tensor_ranges; /* per_tensor only, may be NULL: device {a_max, a_min,
+                                  b_max, b_min} used instead of reducing a and b on the
+                                  device; the max_fp_* / min_fp_* arguments of
+                                  _sc_matmul_per_tensor (kernels.py:1053-1066), e.g.
+                                  global ranges when b is sharded over devices       */
 } scmp_matmul_desc;
 
 /* Bytes of device workspace scmp_sc_matmul needs for `desc` (host-only call). */

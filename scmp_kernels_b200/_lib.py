@@ -38,7 +38,7 @@ class MatmulDesc(ctypes.Structure):
         ("batch", c_int), ("n", c_int), ("m", c_int), ("d", c_int),
         ("a", c_void_p), ("b", c_void_p), ("smooth_scales", c_void_p), ("out", c_void_p),
         ("ktab", c_void_p), ("pattern", c_void_p), ("amap", c_void_p), ("bmap", c_void_p),
-        ("vcap", c_int), ("lp", c_int), ("flags", c_int),
+        ("vcap", c_int), ("lp", c_int), ("flags", c_int), ("tensor_ranges", c_void_p),
     ]
 
 

@@ -241,9 +241,12 @@ int scmp_sc_matmul(const scmp_matmul_desc* d, void* workspace, size_t workspace_
   g.epi.fd = (float)d->d;
 
   if (d->granularity == SCMP_PER_TENSOR) {
-    SCMP_CUDA(launch_row_stats(qa, p.stats_a, st), "per_tensor stats a");
-    SCMP_CUDA(launch_row_stats(qb, p.stats_b, st), "per_tensor stats b");
-    SCMP_CUDA(launch_tensor_params(p.stats_a, qa.rows, p.stats_b, qb.rows, d->d, q, !bip, p.scal, st),
+    if (!d->tensor_ranges) {
+      SCMP_CUDA(launch_row_stats(qa, p.stats_a, st), "per_tensor stats a");
+      SCMP_CUDA(launch_row_stats(qb, p.stats_b, st), "per_tensor stats b");
+    }
+    SCMP_CUDA(launch_tensor_params(p.stats_a, qa.rows, p.stats_b, qb.rows, d->d, q, !bip,
+                                   d->tensor_ranges, p.scal, st),
               "per_tensor params");
     qa.params = qb.params = p.scal;
     qa.param_off = 4;

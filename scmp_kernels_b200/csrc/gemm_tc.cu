@@ -13,39 +13,54 @@
 // an int32 accumulator in tensor memory; epilogue warps read it back with
 // tcgen05.ld and apply the path's float32 recipe. The accumulation is exact.
 //
-// CTA: warps 0-3 expand A' (one a row per thread), warps 4-11 expand B' (one
-// b row per thread), warp 12 allocates tensor memory and issues the MMAs,
-// warps 13-16 run the epilogue. Persistent grid over output tiles. Every
-// mbarrier wait is bounded (common.cuh): on timeout the kernel records
-// SCMP_ERR_TIMEOUT, all roles leave their loops, outstanding MMAs are drained
-// and tensor memory is freed before the CTA exits.
+// Two variants share this code (template parameter PAIR):
+//  - 1 SM per tile (cta_group::1): 128 a rows x 256 b rows per CTA; warps 0-3
+//    expand A' (one a row per thread), warps 4-11 expand B', warp 12 issues
+//    the MMAs, warps 13-16 run the epilogue;
+//  - 2 SMs per tile (cta_group::2, a cluster of two CTAs): 256 a rows x 256 b
+//    rows per pair; each CTA expands its 128 a rows and its half (128 rows)
+//    of B', so a stage moves 64 KB per SM through shared memory instead of
+//    96 KB. The leader CTA (rank 0) issues M=256 MMAs that read both CTAs'
+//    shared memory; producers of both CTAs signal the leader's "full"
+//    barriers, the leader's commits are multicast to both CTAs, and each CTA's
+//    epilogue reads its own 128 rows of the accumulator.
+// Persistent grid over output tiles. Every mbarrier wait is bounded
+// (common.cuh): on timeout the kernel records SCMP_ERR_TIMEOUT, all roles
+// leave their loops, outstanding MMAs are drained and tensor memory is freed
+// before the CTA exits.
 #include "internal.cuh"
 
 namespace scmp {
 namespace tc {
 
-constexpr int BM = 128;                    // a rows per tile (UMMA M)
-constexpr int BN = 256;                    // b rows per tile (UMMA N)
 constexpr int KS = 256;                    // K bytes per stage
-constexpr int NST = 2;                     // pipeline stages
-constexpr int A_BYTES = BM * KS;           // 32 KB
-constexpr int B_BYTES = BN * KS;           // 64 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int A_ATOM = BM * 128;           // one 128-byte-wide K atom of A
-constexpr int B_ATOM = BN * 128;
-constexpr int PROD_A_WARPS = 4, PROD_B_WARPS = 8;
-constexpr int PROD_THREADS = (PROD_A_WARPS + PROD_B_WARPS) * 32;
-constexpr int MMA_WARP = 12;
-constexpr int EPI_WARP0 = 13;
-constexpr int NWARPS = 17;
-constexpr int THREADS = NWARPS * 32;
+constexpr int PROD_A_WARPS = 4;            // 128 a rows per CTA
 constexpr int TMEM_COLS = 512;             // [0,256) accumulator, [256,512) running chunk sum
-constexpr int SMEM_BYTES = NST * STAGE_BYTES + 1024 + 256;
 
-// Instruction descriptor: kind::i8, D = s32, A = B = s8, both K-major,
-// N = 256 (n_dim = N >> 3), M = 128 (m_dim = M >> 4).
-constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                           ((uint32_t)(BM >> 4) << 24);
+template <bool PAIR>
+struct Cfg {
+  static constexpr int BM = 128;                          // a rows per CTA
+  static constexpr int BNL = PAIR ? 128 : 256;            // b rows per CTA
+  static constexpr int TILE_A = PAIR ? 256 : 128;         // a rows per tile
+  static constexpr int TILE_B = 256;                      // b rows per tile (UMMA N)
+  static constexpr int NST = PAIR ? 3 : 2;                // pipeline stages
+  static constexpr int A_BYTES = BM * KS;
+  static constexpr int B_BYTES = BNL * KS;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int A_ATOM = BM * 128;                 // one 128-byte-wide K atom
+  static constexpr int B_ATOM = BNL * 128;
+  static constexpr int PROD_B_WARPS = BNL / 32;
+  static constexpr int PROD_WARPS = PROD_A_WARPS + PROD_B_WARPS;
+  static constexpr int MMA_WARP = PROD_WARPS;
+  static constexpr int EPI_WARP0 = MMA_WARP + 1;
+  static constexpr int NWARPS = EPI_WARP0 + 4;
+  static constexpr int THREADS = NWARPS * 32;
+  static constexpr int SMEM_BYTES = NST * STAGE_BYTES + 1024 + 256;
+  static constexpr int NCTA = PAIR ? 2 : 1;
+  // kind::i8, D = s32, A = B = s8, K-major; N = 256, M = 128 per SM
+  static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TILE_B >> 3) << 17) |
+                                    ((uint32_t)((PAIR ? 256 : 128) >> 4) << 24);
+};
 
 // Shared-memory matrix descriptor, K-major with 128-byte swizzle: rows at a
 // 128-byte pitch, 8-row groups 1024 bytes apart (SBO), version 1.
@@ -63,17 +78,59 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
+template <bool PAIR>
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(acc)
-      : "memory");
+  if constexpr (PAIR) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(Cfg<true>::IDESC), "r"(acc)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(Cfg<false>::IDESC), "r"(acc)
+        : "memory");
+  }
 }
+// Arrive on `bar` (same offset) in every CTA of the tile once all MMAs issued
+// so far by this thread have completed.
+template <bool PAIR>
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-               : "memory");
+  if constexpr (PAIR) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"((uint16_t)0x3)
+        : "memory");
+  } else {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+  }
+}
+// Arrive on the barrier at smem offset `bar` of the tile's leader CTA (rank 0):
+// a local arrive in the leader, a remote one (through mapa) from the peer.
+template <bool PAIR>
+__device__ __forceinline__ void mbar_arrive_leader(uint32_t bar, uint32_t rank) {
+  if (PAIR && rank != 0) {
+    asm volatile(
+        "{\n\t.reg .b32 ra;\n\t"
+        "mapa.shared::cluster.u32 ra, %0, 0;\n\t"
+        "mbarrier.arrive.shared::cluster.b64 _, [ra];\n\t}" ::"r"(bar)
+        : "memory");
+  } else {
+    mbar_arrive(bar);
+  }
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
@@ -107,16 +164,15 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int atom_bytes, int r, in
 }
 
 struct Sched {
-  int tiles, tiles_a, tiles_b, nunits, unit_d, spu_full;  // spu_full: stages of a full unit
+  int tiles, tiles_a, tiles_b, nunits, unit_d, tile_a, tile_b;
 };
 
-__device__ __forceinline__ void tile_coords(const GemmArgs& g, const Sched& s, int tile, int& bh,
-                                            int& a0, int& b0) {
+__device__ __forceinline__ void tile_coords(const Sched& s, int tile, int& bh, int& a0, int& b0) {
   const int per = s.tiles_a * s.tiles_b;
   bh = tile / per;
   const int r = tile % per;
-  a0 = (r / s.tiles_b) * BM;
-  b0 = (r % s.tiles_b) * BN;
+  a0 = (r / s.tiles_b) * s.tile_a;
+  b0 = (r % s.tiles_b) * s.tile_b;
 }
 
 template <int TLEN, int SPD>
@@ -179,162 +235,192 @@ __device__ __forceinline__ int stages_of_unit(int len) {
   return len * (TLEN / 256);
 }
 
+// Producer loop of one operand side. Operands arrive in blocks of eight
+// dimensions: one 16-byte load per thread (its row's signed k or v values,
+// blocked layout) and, for b, two 16-byte loads of the block's table rows.
+// Blocks are fetched one block ahead and b's stream words one stage ahead, so
+// the loads are in flight while the producer waits for its shared-memory
+// slot. Stages are not unrolled (the instruction cache holds both sides'
+// loops); the chunks of a stage are. Returns false after an abort.
+template <bool SIDE_A, int TLEN, int SPD, bool PAIR>
+__device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint32_t sbase, uint32_t bar_base,
+                                        volatile int* abort_flag, uint32_t rank, int tile0, int tstep, int r,
+                                        int lane) {
+  using C = Cfg<PAIR>;
+  constexpr int NST = C::NST;
+  constexpr int DPS = TLEN < 256 ? 256 / TLEN : 1;
+  constexpr int NSPB = SPB<TLEN, SPD>();
+  const int R = SIDE_A ? g.batch * g.n : g.batch * g.m;
+  const uint4* kvsrc = reinterpret_cast<const uint4*>(SIDE_A ? g.ka : g.vb);
+  const int4* bmsrc = reinterpret_cast<const int4*>(g.bmap);
+  const uint32_t LW = (uint32_t)g.lp / 32;
+  uint32_t it = 0;
+  for (int tile = tile0; tile < sc.tiles; tile += tstep) {
+    int bh, a0, b0;
+    tile_coords(sc, tile, bh, a0, b0);
+    const int row = SIDE_A ? a0 + (int)rank * C::BM + r : b0 + (int)rank * C::BNL + r;
+    const bool valid = SIDE_A ? row < g.n : row < g.m;
+    const int grow = bh * (SIDE_A ? g.n : g.m) + (valid ? row : 0);
+    for (int u = 0; u < sc.nunits; ++u) {
+      const int d0 = u * sc.unit_d, d1 = min(d0 + sc.unit_d, g.d);
+      const int nst = stages_of_unit<TLEN>(d1 - d0) * SPD;
+      const int nblk = cdiv(d1 - d0, 8);
+      const int blk0 = d0 >> 3;
+      uint4 kv_cur = valid ? __ldg(kvsrc + (size_t)blk0 * R + grow) : make_uint4(0, 0, 0, 0);
+      int4 bm_lo = make_int4(0, 0, 0, 0), bm_hi = make_int4(0, 0, 0, 0);
+      uint32_t pw[8];
+      if (!SIDE_A) {
+        bm_lo = __ldg(bmsrc + 2 * blk0);
+        bm_hi = __ldg(bmsrc + 2 * blk0 + 1);
+        load_stream_words<TLEN, SPD>(g, kv_cur, bm_lo, bm_hi, 0, d0, d1, valid, LW, pw);
+      }
+      for (int blk = 0; blk < nblk; ++blk) {
+        const int dbase = d0 + 8 * blk;
+        const bool more = blk + 1 < nblk;
+        uint4 kv_nxt = make_uint4(0, 0, 0, 0);
+        int4 nb_lo = make_int4(0, 0, 0, 0), nb_hi = make_int4(0, 0, 0, 0);
+        if (more) {
+          if (valid) kv_nxt = __ldg(kvsrc + (size_t)(blk0 + blk + 1) * R + grow);
+          if (!SIDE_A) {
+            nb_lo = __ldg(bmsrc + 2 * (blk0 + blk + 1));
+            nb_hi = __ldg(bmsrc + 2 * (blk0 + blk + 1) + 1);
+          }
+        }
+        const int jmax = min(NSPB, nst - blk * NSPB);
+#pragma unroll 1
+        for (int j = 0; j < jmax; ++j) {
+          uint32_t pn[8];
+          if (!SIDE_A) {
+            if (j + 1 < NSPB)
+              load_stream_words<TLEN, SPD>(g, kv_cur, bm_lo, bm_hi, j + 1, dbase, d1, valid, LW, pn);
+            else
+              load_stream_words<TLEN, SPD>(g, kv_nxt, nb_lo, nb_hi, 0, dbase + 8, more ? d1 : dbase, valid, LW, pn);
+          }
+          const int s = it % NST;
+          if (!mbar_wait(bar_base + 8u * (NST + s), ((it / NST) & 1) ^ 1, abort_flag, SIDE_A ? 1 : 2))
+            return false;
+          const uint32_t stage = sbase + s * C::STAGE_BYTES + (SIDE_A ? 0 : C::A_BYTES);
+          const int tbase = (j % SPD) * TLEN;
+#pragma unroll
+          for (int dl = 0; dl < DPS; ++dl) {
+            const int e = (j / SPD) * DPS + dl;  // dimension inside the block
+            const int kv = (dbase + e < d1) ? kv_at(kv_cur, e) : 0;
+            const int mag = kv < 0 ? -kv : kv;
+            if (SIDE_A) {
+              const uint32_t fill = kv < 0 ? 0xFFFFFFFFu : 0x01010101u;
+#pragma unroll
+              for (int c = 0; c < TLEN / 16; ++c) {
+                const int r8 = 8 * (mag - tbase - 16 * c);
+                uint32_t w[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const int sh = max(r8 - 32 * q, 0);
+                  w[q] = fill & __funnelshift_lc(0xFFFFFFFFu, 0u, (uint32_t)sh);
+                }
+                st_shared_v4(swz(stage, C::A_ATOM, r, dl * (TLEN / 16) + c), w[0], w[1], w[2], w[3]);
+              }
+            } else {
+              const uint32_t mult = kv < 0 ? 0xFFu : 1u;
+#pragma unroll
+              for (int c = 0; c < TLEN / 16; ++c) {
+                const uint32_t bits = (pw[dl * (TLEN / 32) + (c >> 1)] >> (16 * (c & 1))) & 0xFFFFu;
+                uint32_t w[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const uint32_t nib = (bits >> (4 * q)) & 0xFu;
+                  w[q] = ((nib * 0x00204081u) & 0x01010101u) * mult;
+                }
+                st_shared_v4(swz(stage, C::B_ATOM, r, dl * (TLEN / 16) + c), w[0], w[1], w[2], w[3]);
+              }
+            }
+          }
+          // every lane's stores become visible to the tensor core, then one
+          // lane signals the tile's leader CTA for the whole warp
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_leader<PAIR>(bar_base + 8u * s, rank);
+          ++it;
+          if (!SIDE_A) {
+#pragma unroll
+            for (int x = 0; x < 8; ++x) pw[x] = pn[x];
+          }
+        }
+        kv_cur = kv_nxt;
+        bm_lo = nb_lo;
+        bm_hi = nb_hi;
+      }
+    }
+  }
+  return true;
+}
+
+
 // TLEN: padded stream length lp when lp <= 256 (256/lp dimensions per stage),
-// or 256*k for lp = 256*k (k stages per dimension); here TLEN = min(lp, 256)
-// and SPD = lp / TLEN stages per dimension (1 or 2).
-template <int TLEN, int SPD>
-__global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched sc) {
+// or 256 when lp = 256*SPD (SPD stages per dimension, SPD = 1 or 2).
+template <int TLEN, int SPD, bool PAIR>
+__global__ void __launch_bounds__(Cfg<PAIR>::THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched sc) {
+  using C = Cfg<PAIR>;
+  constexpr int NST = C::NST;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t sbase = (raw + 1023u) & ~1023u;          // SW128 tiles need 1024-B alignment
-  uint8_t* gbase = smem_raw + (sbase - raw);
-  const uint32_t bar_base = sbase + NST * STAGE_BYTES;
+  const uint32_t sbase = (raw + 1023u) & ~1023u;  // SW128 tiles need 1024-B alignment; the
+  uint8_t* gbase = smem_raw + (sbase - raw);      // offset is the same in both CTAs of a pair
+  const uint32_t bar_base = sbase + NST * C::STAGE_BYTES;
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (NST + s); };
   const uint32_t accf_bar = bar_base + 8u * (2 * NST);
   const uint32_t acce_bar = bar_base + 8u * (2 * NST + 1);
   const uint32_t drain_bar = bar_base + 8u * (2 * NST + 2);
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + NST * STAGE_BYTES + 128);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + NST * STAGE_BYTES + 136);
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + NST * C::STAGE_BYTES + 128);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + 136);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int DPS = TLEN < 256 ? 256 / TLEN : 1;  // dimensions per stage
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;   // CTA rank inside the pair
+  const bool leader = rank == 0;
+  const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tstep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
-  if (warp == MMA_WARP) {
+  if (warp == C::MMA_WARP) {
     if (lane == 0) {
       for (int s = 0; s < NST; ++s) {
-        mbar_init(full_bar(s), PROD_THREADS);
+        mbar_init(full_bar(s), C::NCTA * C::PROD_WARPS);  // one arrival per producer warp of the tile
         mbar_init(empty_bar(s), 1);
       }
       mbar_init(accf_bar, 1);
-      mbar_init(acce_bar, 128);
+      mbar_init(acce_bar, C::NCTA * 4);                  // one arrival per epilogue warp of the tile
       mbar_init(drain_bar, 1);
       *abort_flag = 0;
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncwarp();
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32((const void*)tmem_slot)),
-                 "r"(TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if constexpr (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32((const void*)tmem_slot)), "r"(TMEM_COLS) : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32((const void*)tmem_slot)), "r"(TMEM_COLS) : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's barriers exist before anyone arrives on them
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < PROD_A_WARPS + PROD_B_WARPS) {
+  if (warp < C::PROD_WARPS) {
     // ------------------------------------------------------------ producers
-    // Operands arrive in blocks of eight dimensions: one 16-byte load per
-    // thread (its row's signed k or v values, blocked layout) and, for b, two
-    // 16-byte loads of the block's table rows. Blocks are fetched one block
-    // ahead and b's stream words one stage ahead, so the loads are in flight
-    // while the producer waits for its shared-memory slot.
-    const bool side_a = warp < PROD_A_WARPS;
-    const int r = side_a ? threadIdx.x : threadIdx.x - PROD_A_WARPS * 32;
-    const int R = side_a ? g.batch * g.n : g.batch * g.m;
-    const uint4* kvsrc = reinterpret_cast<const uint4*>(side_a ? g.ka : g.vb);
-    const int4* bmsrc = reinterpret_cast<const int4*>(g.bmap);
-    const uint32_t LW = (uint32_t)g.lp / 32;
-    uint32_t it = 0;
-    for (int tile = blockIdx.x; tile < sc.tiles; tile += gridDim.x) {
-      int bh, a0, b0;
-      tile_coords(g, sc, tile, bh, a0, b0);
-      const int row = side_a ? a0 + r : b0 + r;
-      const bool valid = side_a ? row < g.n : row < g.m;
-      const int grow = bh * (side_a ? g.n : g.m) + (valid ? row : 0);
-      for (int u = 0; u < sc.nunits; ++u) {
-        const int d0 = u * sc.unit_d, d1 = min(d0 + sc.unit_d, g.d);
-        const int nst = stages_of_unit<TLEN>(d1 - d0) * SPD;
-        const int nblk = cdiv(d1 - d0, 8);
-        const int blk0 = d0 >> 3;
-        uint4 kv_cur = valid ? __ldg(kvsrc + (size_t)blk0 * R + grow) : make_uint4(0, 0, 0, 0);
-        int4 bm_lo = make_int4(0, 0, 0, 0), bm_hi = make_int4(0, 0, 0, 0);
-        if (!side_a) {
-          bm_lo = __ldg(bmsrc + 2 * blk0);
-          bm_hi = __ldg(bmsrc + 2 * blk0 + 1);
-        }
-        uint32_t pw[8];
-        if (!side_a) load_stream_words<TLEN, SPD>(g, kv_cur, bm_lo, bm_hi, 0, d0, d1, valid, LW, pw);
-        for (int blk = 0; blk < nblk; ++blk) {
-          const int dbase = d0 + 8 * blk;
-          const bool more = blk + 1 < nblk;
-          uint4 kv_nxt = make_uint4(0, 0, 0, 0);
-          int4 nb_lo = make_int4(0, 0, 0, 0), nb_hi = make_int4(0, 0, 0, 0);
-          if (more) {
-            if (valid) kv_nxt = __ldg(kvsrc + (size_t)(blk0 + blk + 1) * R + grow);
-            if (!side_a) {
-              nb_lo = __ldg(bmsrc + 2 * (blk0 + blk + 1));
-              nb_hi = __ldg(bmsrc + 2 * (blk0 + blk + 1) + 1);
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < SPB<TLEN, SPD>(); ++j) {
-            if (blk * SPB<TLEN, SPD>() + j >= nst) break;
-            uint32_t pn[8];
-            if (!side_a) {
-              if (j + 1 < SPB<TLEN, SPD>())
-                load_stream_words<TLEN, SPD>(g, kv_cur, bm_lo, bm_hi, j + 1, dbase, d1, valid, LW, pn);
-              else
-                load_stream_words<TLEN, SPD>(g, kv_nxt, nb_lo, nb_hi, 0, dbase + 8, more ? d1 : dbase, valid, LW, pn);
-            }
-            const int s = it % NST;
-            if (!mbar_wait(empty_bar(s), ((it / NST) & 1) ^ 1, abort_flag, side_a ? 1 : 2)) goto done;
-            const uint32_t stage = sbase + s * STAGE_BYTES;
-            const int tbase = (j % SPD) * TLEN;
-#pragma unroll
-            for (int dl = 0; dl < DPS; ++dl) {
-              const int e = (j / SPD) * DPS + dl;  // dimension inside the block
-              const int kv = (dbase + e < d1) ? kv_at(kv_cur, e) : 0;
-              const int mag = kv < 0 ? -kv : kv;
-              if (side_a) {
-                const uint32_t fill = kv < 0 ? 0xFFFFFFFFu : 0x01010101u;
-#pragma unroll
-                for (int c = 0; c < TLEN / 16; ++c) {
-                  const int r8 = 8 * (mag - tbase - 16 * c);
-                  uint32_t w[4];
-#pragma unroll
-                  for (int q = 0; q < 4; ++q) {
-                    const int sh = max(r8 - 32 * q, 0);
-                    w[q] = fill & __funnelshift_lc(0xFFFFFFFFu, 0u, (uint32_t)sh);
-                  }
-                  st_shared_v4(swz(stage, A_ATOM, r, dl * (TLEN / 16) + c), w[0], w[1], w[2], w[3]);
-                }
-              } else {
-                const uint32_t mult = kv < 0 ? 0xFFu : 1u;
-#pragma unroll
-                for (int c = 0; c < TLEN / 16; ++c) {
-                  const uint32_t bits = (pw[dl * (TLEN / 32) + (c >> 1)] >> (16 * (c & 1))) & 0xFFFFu;
-                  uint32_t w[4];
-#pragma unroll
-                  for (int q = 0; q < 4; ++q) {
-                    const uint32_t nib = (bits >> (4 * q)) & 0xFu;
-                    w[q] = ((nib * 0x00204081u) & 0x01010101u) * mult;
-                  }
-                  st_shared_v4(swz(stage + A_BYTES, B_ATOM, r, dl * (TLEN / 16) + c), w[0], w[1], w[2], w[3]);
-                }
-              }
-            }
-            fence_proxy_async();
-            mbar_arrive(full_bar(s));
-            ++it;
-            if (!side_a) {
-#pragma unroll
-              for (int x = 0; x < 8; ++x) pw[x] = pn[x];
-            }
-          }
-          kv_cur = kv_nxt;
-          bm_lo = nb_lo;
-          bm_hi = nb_hi;
-        }
-      }
-    }
-  } else if (warp == MMA_WARP) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (warp < PROD_A_WARPS)
+      produce<true, TLEN, SPD, PAIR>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep, threadIdx.x, lane);
+    else
+      produce<false, TLEN, SPD, PAIR>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep,
+                                      threadIdx.x - PROD_A_WARPS * 32, lane);
+  } else if (warp == C::MMA_WARP) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA)
+    if (lane == 0 && leader) {
       uint32_t it = 0, uc = 0;
-      for (int tile = blockIdx.x; tile < sc.tiles; tile += gridDim.x) {
+      for (int tile = tile0; tile < sc.tiles; tile += tstep) {
         for (int u = 0; u < sc.nunits; ++u, ++uc) {
           if (!mbar_wait(acce_bar, (uc & 1) ^ 1, abort_flag, 4)) goto mma_done;
           tc_fence_after();
@@ -344,22 +430,27 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched s
             const int s = it % NST;
             if (!mbar_wait(full_bar(s), (it / NST) & 1, abort_flag, 3)) goto mma_done;
             tc_fence_after();
-            const uint32_t a_base = sbase + s * STAGE_BYTES, b_base = a_base + A_BYTES;
+            const uint32_t a_base = sbase + s * C::STAGE_BYTES, b_base = a_base + C::A_BYTES;
 #pragma unroll
             for (int kk = 0; kk < KS / 32; ++kk) {
               const uint32_t off = (kk & 3) * 32;
-              mma_i8(tmem, smem_desc(a_base + (kk >> 2) * A_ATOM + off),
-                     smem_desc(b_base + (kk >> 2) * B_ATOM + off), (st > 0 || kk > 0) ? 1u : 0u);
+              mma_i8<PAIR>(tmem, smem_desc(a_base + (kk >> 2) * C::A_ATOM + off),
+                           smem_desc(b_base + (kk >> 2) * C::B_ATOM + off), (st > 0 || kk > 0) ? 1u : 0u);
             }
-            mma_commit(empty_bar(s));
+            mma_commit<PAIR>(empty_bar(s));
           }
-          mma_commit(accf_bar);
+          mma_commit<PAIR>(accf_bar);
         }
       }
     mma_done:
       // drain: completes once every MMA issued above has finished; waited on
       // even after an abort, so tensor memory is never freed under a live MMA
-      mma_commit(drain_bar);
+      if constexpr (PAIR) {
+        asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(drain_bar)
+                     : "memory");
+      } else {
+        mma_commit<false>(drain_bar);
+      }
       {
         int zero = 0;
         mbar_wait(drain_bar, 0, &zero, 6);
@@ -371,17 +462,17 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched s
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16);
     uint32_t uc = 0;
-    for (int tile = blockIdx.x; tile < sc.tiles; tile += gridDim.x) {
+    for (int tile = tile0; tile < sc.tiles; tile += tstep) {
       int bh, a0, b0;
-      tile_coords(g, sc, tile, bh, a0, b0);
-      const int ia = a0 + 32 * q + lane;
+      tile_coords(sc, tile, bh, a0, b0);
+      const int ia = a0 + (int)rank * C::BM + 32 * q + lane;
       const bool chunked = g.epi.kind == EPI_CHUNK;
       for (int u = 0; u < sc.nunits; ++u, ++uc) {
         if (!mbar_wait(accf_bar, uc & 1, abort_flag, 5)) goto done;
         tc_fence_after();
         const bool last = u == sc.nunits - 1;
 #pragma unroll 1
-        for (int cb = 0; cb < BN / 16; ++cb) {
+        for (int cb = 0; cb < C::TILE_B / 16; ++cb) {
           uint32_t acc[16], run[16];
           TMEM_LD16(lane_addr + cb * 16, acc);
           if (chunked && u > 0) TMEM_LD16(lane_addr + 256 + cb * 16, run);
@@ -410,31 +501,57 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched s
         }
         if (chunked && !last) tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(acce_bar);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar, rank);
       }
     }
   }
 done:
   tc_fence_before();
   __syncthreads();
-  if (warp == MMA_WARP) {
+  if constexpr (PAIR) cluster_sync();  // no CTA leaves while its peer may still touch it
+  if (warp == C::MMA_WARP) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS)
-                 : "memory");
+    if constexpr (PAIR) {
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS)
+                   : "memory");
+    } else {
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS)
+                   : "memory");
+    }
   }
 }
 
-template <int TLEN, int SPD>
-static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int grid, cudaStream_t st) {
+template <int TLEN, int SPD, bool PAIR>
+static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int sms, cudaStream_t st) {
+  using C = Cfg<PAIR>;
   static bool attr = false;
+  auto kern = gemm_tc_kernel<TLEN, SPD, PAIR>;
   if (!attr) {
-    cudaError_t e =
-        cudaFuncSetAttribute(gemm_tc_kernel<TLEN, SPD>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  gemm_tc_kernel<TLEN, SPD><<<grid, THREADS, SMEM_BYTES, st>>>(g, s);
-  return cudaGetLastError();
+  if constexpr (!PAIR) {
+    const int grid = s.tiles < sms ? s.tiles : sms;
+    kern<<<grid, C::THREADS, C::SMEM_BYTES, st>>>(g, s);
+    return cudaGetLastError();
+  } else {
+    const int pairs = s.tiles < sms / 2 ? s.tiles : sms / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(C::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, g, s);
+  }
 }
 
 }  // namespace tc
@@ -452,25 +569,42 @@ bool gemm_tc_supported(const GemmArgs& g) {
   return major == 10 && minor == 0;
 }
 
+// The 2-SM variant is the default; SCMP_TC_SINGLE=1 in the environment selects
+// the 1-SM variant (kept for comparison and as a fallback).
+static bool use_pair() {
+  const char* e = getenv("SCMP_TC_SINGLE");
+  return !(e && e[0] == '1');
+}
+
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
   using namespace tc;
+  const bool pair = use_pair();
   Sched s{};
-  s.tiles_a = cdiv(g.n, BM);
-  s.tiles_b = cdiv(g.m, BN);
+  s.tile_a = pair ? Cfg<true>::TILE_A : Cfg<false>::TILE_A;
+  s.tile_b = 256;
+  s.tiles_a = cdiv(g.n, s.tile_a);
+  s.tiles_b = cdiv(g.m, s.tile_b);
   s.tiles = g.batch * s.tiles_a * s.tiles_b;
   s.unit_d = g.unit_d > 0 ? g.unit_d : g.d;
   s.nunits = cdiv(g.d, s.unit_d);
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int grid = s.tiles < sms ? s.tiles : sms;
   const int tlen = g.lp < 256 ? g.lp : 256;
   const int spd = g.lp / tlen;
+  if (pair) {
+    switch (tlen) {
+      case 32: return launch_t<32, 1, true>(g, s, sms, st);
+      case 64: return launch_t<64, 1, true>(g, s, sms, st);
+      case 128: return launch_t<128, 1, true>(g, s, sms, st);
+      default: return spd == 2 ? launch_t<256, 2, true>(g, s, sms, st) : launch_t<256, 1, true>(g, s, sms, st);
+    }
+  }
   switch (tlen) {
-    case 32: return launch_t<32, 1>(g, s, grid, st);
-    case 64: return launch_t<64, 1>(g, s, grid, st);
-    case 128: return launch_t<128, 1>(g, s, grid, st);
-    default: return spd == 2 ? launch_t<256, 2>(g, s, grid, st) : launch_t<256, 1>(g, s, grid, st);
+    case 32: return launch_t<32, 1, false>(g, s, sms, st);
+    case 64: return launch_t<64, 1, false>(g, s, sms, st);
+    case 128: return launch_t<128, 1, false>(g, s, sms, st);
+    default: return spd == 2 ? launch_t<256, 2, false>(g, s, sms, st) : launch_t<256, 1, false>(g, s, sms, st);
   }
 }
 

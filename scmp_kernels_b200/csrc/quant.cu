@@ -144,18 +144,32 @@ __global__ void group_params_kernel(const float* __restrict__ stats, int rpb, in
 //   scal[1] = fl32(-zp_b)                    scal[5] = fl32(inv_scale_b)
 //   scal[2] = fl32(zp_a)                     scal[6] = fl32(zp_a)  (quant offset)
 //   scal[3] = fl32(D * zp_a * zp_b)          scal[7] = fl32(zp_b)
+// `ranges` (optional) = {a_max, a_min, b_max, b_min} given by the caller.
 __global__ void tensor_params_kernel(const float* __restrict__ stats_a, int rows_a,
                                      const float* __restrict__ stats_b, int rows_b, int d, int q,
-                                     int unipolar, float* __restrict__ scal) {
-  float am_a, mx_a, mn_a, am_b, mx_b, mn_b;
-  group_reduce(stats_a, 0, rows_a, am_a, mx_a, mn_a);
-  group_reduce(stats_b, 0, rows_b, am_b, mx_b, mn_b);
+                                     int unipolar, const double* __restrict__ ranges,
+                                     float* __restrict__ scal) {
+  double mx_a, mn_a, mx_b, mn_b;
+  if (ranges) {
+    mx_a = ranges[0];
+    mn_a = ranges[1];
+    mx_b = ranges[2];
+    mn_b = ranges[3];
+  } else {
+    float am, x, n;
+    group_reduce(stats_a, 0, rows_a, am, x, n);
+    mx_a = x;
+    mn_a = n;
+    group_reduce(stats_b, 0, rows_b, am, x, n);
+    mx_b = x;
+    mn_b = n;
+  }
   if (threadIdx.x != 0) return;
   const double qd = (double)q;
   if (!unipolar) {
     // abs_max = max(|max|, |min|, 1e-5); scale = abs_max / q; inv = 1 / scale
-    const double aa = fmax(fmax(fabs((double)mx_a), fabs((double)mn_a)), 1e-5);
-    const double ab = fmax(fmax(fabs((double)mx_b), fabs((double)mn_b)), 1e-5);
+    const double aa = fmax(fmax(fabs(mx_a), fabs(mn_a)), 1e-5);
+    const double ab = fmax(fmax(fabs(mx_b), fabs(mn_b)), 1e-5);
     const double sa = aa / qd, sb = ab / qd;
     scal[0] = (float)(sa * sb);
     scal[4] = (float)(1.0 / sa);
@@ -164,11 +178,11 @@ __global__ void tensor_params_kernel(const float* __restrict__ stats_a, int rows
   } else {
     // range = max(max - min, 1e-5); scale = range / q; inv = 1 / scale;
     // zp = clamp(round(-min / scale), 0, q)
-    const double ra = fmax((double)mx_a - (double)mn_a, 1e-5);
-    const double rb = fmax((double)mx_b - (double)mn_b, 1e-5);
+    const double ra = fmax(mx_a - mn_a, 1e-5);
+    const double rb = fmax(mx_b - mn_b, 1e-5);
     const double sa = ra / qd, sb = rb / qd;
-    const double za = fmax(0.0, fmin(qd, rint(-(double)mn_a / sa)));
-    const double zb = fmax(0.0, fmin(qd, rint(-(double)mn_b / sb)));
+    const double za = fmax(0.0, fmin(qd, rint(-mn_a / sa)));
+    const double zb = fmax(0.0, fmin(qd, rint(-mn_b / sb)));
     scal[0] = (float)(sa * sb);
     scal[1] = (float)(-zb);
     scal[2] = (float)za;
@@ -303,8 +317,8 @@ cudaError_t launch_group_params(const float* stats, int batch, int rpb, int G, i
 }
 
 cudaError_t launch_tensor_params(const float* sa, int ra, const float* sb, int rb, int d, int q,
-                                 int unipolar, float* scal, cudaStream_t st) {
-  tensor_params_kernel<<<1, 1024, 0, st>>>(sa, ra, sb, rb, d, q, unipolar, scal);
+                                 int unipolar, const double* ranges, float* scal, cudaStream_t st) {
+  tensor_params_kernel<<<1, 1024, 0, st>>>(sa, ra, sb, rb, d, q, unipolar, ranges, scal);
   return cudaGetLastError();
 }
 

@@ -46,7 +46,7 @@ cudaError_t launch_row_stats(const QuantArgs& q, float* stats, cudaStream_t st);
 cudaError_t launch_group_params(const float* stats, int batch, int rpb, int G, int q, int recipe,
                                 float* scale, float* zp, cudaStream_t st);
 cudaError_t launch_tensor_params(const float* sa, int ra, const float* sb, int rb, int d, int q,
-                                 int unipolar, float* scal, cudaStream_t st);
+                                 int unipolar, const double* ranges, float* scal, cudaStream_t st);
 cudaError_t launch_quant_rows(int recipe, const QuantArgs& q, cudaStream_t st);
 
 }  // namespace scmp

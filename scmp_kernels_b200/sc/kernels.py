@@ -249,7 +249,8 @@ def _to_device(x: torch.Tensor) -> torch.Tensor:
 def _launch(gran: int, mode: str, a: torch.Tensor, b: torch.Tensor, sc_prec: int, tables: EnableTables,
             *, group_a=1, group_b=1, chunk_d=0, smooth: Optional[torch.Tensor] = None,
             period: Optional[int] = None, out: Optional[torch.Tensor] = None,
-            workspace: Optional[torch.Tensor] = None, flags: int = 0) -> torch.Tensor:
+            workspace: Optional[torch.Tensor] = None, flags: int = 0,
+            ranges: Optional[torch.Tensor] = None) -> torch.Tensor:
     """One ``scmp_sc_matmul`` call. a: (batch, n, d) or (n, d); b likewise."""
     three_d = a.dim() == 3
     batch = a.shape[0] if three_d else 1
@@ -266,7 +267,8 @@ def _launch(gran: int, mode: str, a: torch.Tensor, b: torch.Tensor, sc_prec: int
         a=a.data_ptr(), b=b.data_ptr(), smooth_scales=smooth.data_ptr() if smooth is not None else None,
         out=out.data_ptr(), ktab=tables.ktab.data_ptr(), pattern=tables.pattern.data_ptr(),
         amap=amap.data_ptr(), bmap=bmap.data_ptr(), vcap=tables.vcap, lp=tables.lp,
-        flags=flags | (_lib.FLAG_FORCE_SIMT if _FORCE_SIMT else 0))
+        flags=flags | (_lib.FLAG_FORCE_SIMT if _FORCE_SIMT else 0),
+        tensor_ranges=ranges.data_ptr() if ranges is not None else None)
     L = _lib.lib()
     ws_bytes = ctypes.c_size_t(0)
     _lib.check(L.scmp_sc_matmul_workspace_size(ctypes.byref(desc), ctypes.byref(ws_bytes)), "sc_matmul")
@@ -299,10 +301,15 @@ def _default_config(config, D, sc_prec):
 
 
 @torch.no_grad()
-def _sc_matmul_per_tensor(a, b, mode="bipolar", sc_prec=8, config=None, stoc_len=None,
-                          rng_levels=None, smooth_scales=None, flags=0):
-    """per_tensor path (kernels.py:1053-1226). Ranges and scales are reduced on
-    the device (the reference reads them back with .item())."""
+def _sc_matmul_per_tensor(a, b, max_fp_a=None, min_fp_a=None, max_fp_b=None, min_fp_b=None,
+                          mode="bipolar", sc_prec=8, config=None, stoc_len=None, rng_levels=None,
+                          smooth_scales=None, flags=0):
+    """per_tensor path (kernels.py:1053-1226). Without explicit ranges the
+    tensors' max/min are reduced on the device (sc_matmul's reference reads them
+    back with .item(), matmul.py:227-230); with ``max_fp_a`` / ``min_fp_a``
+    (and optionally ``max_fp_b`` / ``min_fp_b``, defaulting to a's, as in
+    kernels.py:1092-1095) those host values are used, e.g. global ranges when
+    b is sharded over devices."""
     assert a.dim() == b.dim() and a.dim() in (2, 3), f"Expected 2D, got a:{a.dim()}D b:{b.dim()}D"
     assert a.shape[-1] == b.shape[-1], f"Dim mismatch: a={a.shape[-1]}, b={b.shape[-1]}"
     a, b, s = _prep_smooth(a, b, smooth_scales)
@@ -311,7 +318,15 @@ def _sc_matmul_per_tensor(a, b, mode="bipolar", sc_prec=8, config=None, stoc_len
     D = a.shape[-1]
     config = _default_config(config, D, sc_prec)
     t = _get_cached_enable_tables(config, sc_prec, a.device, stoc_len, rng_levels)
-    y = _launch(_lib.PER_TENSOR, mode, a, b, sc_prec, t, smooth=s, flags=flags)
+    ranges = None
+    if max_fp_a is not None or min_fp_a is not None:
+        if max_fp_a is None or min_fp_a is None:
+            raise ValueError("_sc_matmul_per_tensor: give both max_fp_a and min_fp_a")
+        mb = max_fp_a if max_fp_b is None else max_fp_b
+        nb = min_fp_a if min_fp_b is None else min_fp_b
+        ranges = torch.tensor([float(max_fp_a), float(min_fp_a), float(mb), float(nb)],
+                              dtype=torch.float64).to(a.device, non_blocking=True)
+    y = _launch(_lib.PER_TENSOR, mode, a, b, sc_prec, t, smooth=s, flags=flags, ranges=ranges)
     return y if dev_in.type == "cuda" else y.to(dev_in)
 
 

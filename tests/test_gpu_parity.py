@@ -28,9 +28,14 @@ from scmp_kernels_b200.sc import kernels as K  # noqa: E402
 DEV = "cuda:0"
 
 
-@pytest.fixture(params=["tc", "simt"])
+@pytest.fixture(params=["tc2", "tc1", "simt"])
 def impl(request, monkeypatch):
+    """tc2: tcgen05 on SM pairs (default); tc1: tcgen05 on single SMs; simt: CUDA cores."""
     monkeypatch.setattr(K, "_FORCE_SIMT", request.param == "simt")
+    if request.param == "tc1":
+        monkeypatch.setenv("SCMP_TC_SINGLE", "1")
+    else:
+        monkeypatch.delenv("SCMP_TC_SINGLE", raising=False)
     clear_rng_cache()
     yield request.param
     clear_rng_cache()
@@ -113,16 +118,23 @@ def test_random_vs_oracle(case, impl, env_vars):
     assert np.array_equal(y, ref), f"max |diff| {np.abs(y - ref).max()}"
 
 
-def test_tc_matches_simt_at_size(monkeypatch, env_vars):
+@pytest.mark.parametrize("shape,kw", [
+    ((300, 520, 1000), dict(granularity="per_row", sc_prec=8)),
+    ((700, 1300, 512), dict(granularity="per_row", mode="unipolar", sc_prec=6, stoc_len=64)),
+    ((260, 600, 640), dict(granularity="per_row", sc_prec=8, chunk_d=64, stoc_len=128, rng_levels=128)),
+])
+def test_tc_variants_match_simt_at_size(shape, kw, monkeypatch, env_vars):
     env_vars({})
+    n, m, d = shape
     g = torch.Generator(device=DEV).manual_seed(7)
-    a = torch.randn(300, 1000, device=DEV, generator=g)
-    b = torch.randn(520, 1000, device=DEV, generator=g) * 0.02
+    a = torch.randn(n, d, device=DEV, generator=g)
+    b = torch.randn(m, d, device=DEV, generator=g) * 0.02
     outs = []
-    for simt in (False, True):
+    for simt, single in ((True, "0"), (False, "0"), (False, "1")):
         monkeypatch.setattr(K, "_FORCE_SIMT", simt)
-        outs.append(sc_matmul(a, b, "per_row", sc_prec=8))
-    assert torch.equal(outs[0], outs[1])
+        monkeypatch.setenv("SCMP_TC_SINGLE", single)
+        outs.append(sc_matmul(a, b, **kw))
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
     assert _lib.device_error() == 0
 
 
