@@ -59,11 +59,16 @@ enum scmp_mode { SCMP_BIPOLAR = 0, SCMP_UNIPOLAR = 1 };
  *   rb: (n_rb, L) int32   sequences of operand b ("k" side)
  * Outputs, for v in [0, vcap]:
  *   ktab:    (n_ra, vcap+1) int16   ktab[r][v] = #{t < L : ra[r][t] < v}
- *   pattern: (n_rb, vcap+1, lp/32) uint32, bit t of row (r, v) set iff
- *            t < L and rb[r][t] < v  (the comparator stream of b, bit-packed)
+ *   pattern: (n_rb, vcap+1, lp/32) uint32, the comparator stream of b,
+ *            bit-packed: position t of row (r, v) is set iff t < L and
+ *            rb[r][t] < v. Word w holds positions 32w..32w+31 in "sliced"
+ *            order: position 32w + 16h + 4q + i at bit 8i + 4h + q (h < 2,
+ *            q, i < 4), so that one shift and one mask of a word yield four
+ *            consecutive positions as the bytes of an int8 operand word.
  * lp >= L is the padded stream length (a multiple of 32). Every sequence value
  * must be < vcap, so that boundaries >= vcap saturate (ktab = L, all bits set).
- * The reference's cum_indicator[d][k][v] equals popcount(pattern[d][v] & (2^k - 1)).
+ * The reference's cum_indicator[d][k][v] equals the number of set positions t < k of
+ * pattern[d][v].
  */
 int scmp_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, int n_rb, int L, int lp,
                       int vcap, int16_t* ktab, uint32_t* pattern, void* stream);

@@ -2,7 +2,8 @@
 //
 // S[i][j] = sum_d sa*sb * popcount(pattern[bmap[d]][v[j][d]] & (2^k[i][d] - 1))
 // i.e. the reference's cum_indicator[d][k][v] lookup (sc/kernels.py:229-236)
-// evaluated as a prefix popcount of b's bit-packed comparator stream. Each
+// evaluated as a prefix popcount of b's bit-packed comparator stream (words
+// put back in position order when staged). Each
 // 64x64 output tile stages, per dimension, every b row's stream words and
 // their running popcounts in shared memory, so one popc serves one MAC.
 // Used for shapes the tcgen05 kernel does not take and as its cross-check.
@@ -68,7 +69,7 @@ __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(GemmArgs g) {
           const uint32_t* src =
               g.pattern + ((size_t)__ldg(g.bmap + d) * (g.vcap + 1) + v) * lw;
           for (int x = 0; x < lw; ++x) {
-            const uint32_t bits = __ldg(src + x);
+            const uint32_t bits = unslice(__ldg(src + x));
             w[x] = bits;
             p[x] = acc;
             acc += __popc(bits);

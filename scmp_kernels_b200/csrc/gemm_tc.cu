@@ -157,12 +157,6 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Byte address of 16-byte chunk `kc` (0..15 within the stage's 256 K bytes)
-// of row `r` in a K-major SW128 tile with `atom_bytes` per 128-byte K atom.
-__device__ __forceinline__ uint32_t swz(uint32_t base, int atom_bytes, int r, int kc) {
-  return base + (kc >> 3) * atom_bytes + r * 128 + ((((kc & 7) ^ (r & 7))) << 4);
-}
-
 struct Sched {
   int tiles, tiles_a, tiles_b, nunits, unit_d, tile_a, tile_b;
 };
@@ -254,6 +248,10 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
   const uint4* kvsrc = reinterpret_cast<const uint4*>(SIDE_A ? g.ka : g.vb);
   const int4* bmsrc = reinterpret_cast<const int4*>(g.bmap);
   const uint32_t LW = (uint32_t)g.lp / 32;
+  // byte offset of 16-byte chunk k (0..7) of row r in a 128-byte-swizzled atom
+  uint32_t xo[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) xo[k] = (uint32_t)r * 128u + (uint32_t)((k ^ (r & 7)) << 4);
   uint32_t it = 0;
   for (int tile = tile0; tile < sc.tiles; tile += tstep) {
     int bh, a0, b0;
@@ -307,30 +305,32 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
             const int kv = (dbase + e < d1) ? kv_at(kv_cur, e) : 0;
             const int mag = kv < 0 ? -kv : kv;
             if (SIDE_A) {
+              // word x of the piece holds positions 4x..4x+3: its low
+              // clamp(mag - tbase - 4x, 0, 4) bytes are `fill`, i.e. the top
+              // bytes of (0:fill) << max(8*(mag - tbase) - 32x, 0), clamped at 32
               const uint32_t fill = kv < 0 ? 0xFFFFFFFFu : 0x01010101u;
+              const int sh = 8 * (mag - tbase);
 #pragma unroll
               for (int c = 0; c < TLEN / 16; ++c) {
-                const int r8 = 8 * (mag - tbase - 16 * c);
                 uint32_t w[4];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  const int sh = max(r8 - 32 * q, 0);
-                  w[q] = fill & __funnelshift_lc(0xFFFFFFFFu, 0u, (uint32_t)sh);
-                }
-                st_shared_v4(swz(stage, C::A_ATOM, r, dl * (TLEN / 16) + c), w[0], w[1], w[2], w[3]);
+                for (int q = 0; q < 4; ++q)
+                  w[q] = __funnelshift_lc(fill, 0u, (uint32_t)max(sh - 32 * (4 * c + q), 0));
+                const int kc = dl * (TLEN / 16) + c;
+                st_shared_v4(stage + (kc >> 3) * C::A_ATOM + xo[kc & 7], w[0], w[1], w[2], w[3]);
               }
             } else {
+              // sliced stream words: chunk c's four words are the bytes'
+              // bit 0 of (word >> (4*(c&1) + q)), negated for v < 0
               const uint32_t mult = kv < 0 ? 0xFFu : 1u;
 #pragma unroll
               for (int c = 0; c < TLEN / 16; ++c) {
-                const uint32_t bits = (pw[dl * (TLEN / 32) + (c >> 1)] >> (16 * (c & 1))) & 0xFFFFu;
+                const uint32_t sw = pw[dl * (TLEN / 32) + (c >> 1)];
                 uint32_t w[4];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  const uint32_t nib = (bits >> (4 * q)) & 0xFu;
-                  w[q] = ((nib * 0x00204081u) & 0x01010101u) * mult;
-                }
-                st_shared_v4(swz(stage, C::B_ATOM, r, dl * (TLEN / 16) + c), w[0], w[1], w[2], w[3]);
+                for (int q = 0; q < 4; ++q) w[q] = ((sw >> (4 * (c & 1) + q)) & 0x01010101u) * mult;
+                const int kc = dl * (TLEN / 16) + c;
+                st_shared_v4(stage + (kc >> 3) * C::B_ATOM + xo[kc & 7], w[0], w[1], w[2], w[3]);
               }
             }
           }

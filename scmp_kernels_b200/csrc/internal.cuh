@@ -74,6 +74,25 @@ __host__ __device__ __forceinline__ size_t blk_idx(int R, int row, int j) {
   return ((size_t)(j >> 3) * R + row) * 8 + (j & 7);
 }
 
+// Bit order of the 32-bit comparator-stream words ("sliced"): stream
+// position 16h + 4q + i of a word (h < 2, q < 4, i < 4) sits at bit
+// 8i + 4h + q, so the four positions 16h+4q .. 16h+4q+3 are bit 0 of the four
+// bytes of (word >> (4h + q)): one shift and one mask give four int8 stream
+// values. slice_bit(l) is the bit of position l; unslice() restores position
+// order (bit l = position l).
+__host__ __device__ constexpr int slice_bit(int l) { return 8 * (l & 3) + 4 * (l >> 4) + ((l >> 2) & 3); }
+__device__ __forceinline__ uint32_t unslice(uint32_t w) {
+  uint32_t lin = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {  // k = 4h + q: positions 4k .. 4k+3
+    const uint32_t x = (w >> k) & 0x01010101u;
+    // bytes' bit 0 (bits 0, 8, 16, 24) gathered into bits 24..27 by one
+    // multiply: partial products land on distinct bits, so nothing carries
+    lin |= (((x * 0x01020408u) >> 24) & 0xFu) << (4 * k);
+  }
+  return lin;
+}
+
 // SC-GEMM operands and epilogue.
 //   ka: signed thermometer length sa * k of operand a, blocked (R = batch*n);
 //   vb: signed boundary sb * v of operand b, blocked (R = batch*m);

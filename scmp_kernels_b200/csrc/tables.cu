@@ -26,7 +26,7 @@ __global__ void k_table_kernel(const int32_t* __restrict__ ra, int L, int vcap,
   }
 }
 
-// pattern[r][v][w] bit i = (32w + i < L) && rb[r][32w + i] < v
+// pattern[r][v][w] bit slice_bit(i) = (32w + i < L) && rb[r][32w + i] < v
 __global__ void pattern_kernel(const int32_t* __restrict__ rb, int L, int lp, int vcap,
                                uint32_t* __restrict__ pat) {
   extern __shared__ int32_t srow[];
@@ -40,7 +40,7 @@ __global__ void pattern_kernel(const int32_t* __restrict__ rb, int L, int lp, in
     uint32_t bits = 0;
     for (int i = 0; i < 32; ++i) {
       const int t = 32 * w + i;
-      if (t < L && srow[t] < v) bits |= 1u << i;
+      if (t < L && srow[t] < v) bits |= 1u << slice_bit(i);
     }
     pat[((size_t)r * (vcap + 1) + v) * lw + w] = bits;
   }

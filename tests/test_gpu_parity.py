@@ -77,7 +77,12 @@ def test_device_tables_reproduce_reference(L, G, env_vars):
     ref_k = RNG[f"ktab_L{L}_G{G}"]
     assert np.array_equal(kt[:, :G + 1], ref_k[:, :G + 1])
     pat = t.pattern.cpu().numpy().view(np.uint32)[t.bmap.cpu().numpy()]   # (6, vcap+1, lw)
-    bits = np.unpackbits(pat.view(np.uint8), axis=-1, bitorder="little")  # (6, vcap+1, lp)
+    sliced = np.unpackbits(pat.view(np.uint8), axis=-1, bitorder="little")  # (6, vcap+1, lp), bit order
+    # word bit 8i + 4h + q holds position 16h + 4q + i of the word
+    l = np.arange(32)
+    perm = 8 * (l & 3) + 4 * (l >> 4) + ((l >> 2) & 3)
+    idx = (np.arange(sliced.shape[-1]) // 32) * 32 + perm[np.arange(sliced.shape[-1]) % 32]
+    bits = sliced[..., idx]                                               # position order
     cum = np.concatenate([np.zeros(bits.shape[:2] + (1,), np.int64), np.cumsum(bits, -1)], -1)
     ref = RNG[f"cum_L{L}_G{G}"]                                           # (6, L+1, V)
     vv = min(ref.shape[2], t.vcap + 1)
@@ -96,6 +101,7 @@ CASES = [
     dict(granularity="per_head", mode="bipolar", sc_prec=8, bh=3, n=23, m=41, d=19),
     dict(granularity="per_row", mode="bipolar", sc_prec=8, bh=2, n=9, m=140, d=31, stoc_len=32),
     dict(granularity="per_row", mode="bipolar", sc_prec=5, n=140, m=270, d=48, stoc_len=20),
+    dict(granularity="per_row", mode="bipolar", sc_prec=9, n=40, m=270, d=24),
 ]
 
 
