@@ -45,6 +45,8 @@ enum scmp_mode { SCMP_BIPOLAR = 0, SCMP_UNIPOLAR = 1 };
 
 /* scmp_matmul_desc.flags */
 #define SCMP_FLAG_FORCE_SIMT 0x1 /* use the CUDA-core GEMM instead of tcgen05  */
+#define SCMP_FLAG_NO_SPLIT 0x2   /* do not split the last wave of output tiles
+                                    over K (smaller workspace, longer tail)     */
 
 /*
  * Enable-signal tables (the "RNG cache" kept resident in HBM).

@@ -25,6 +25,7 @@ SCMP_ERR_WORKSPACE = 5
 PER_TENSOR, PER_ROW, PER_HEAD = 0, 1, 2
 BIPOLAR, UNIPOLAR = 0, 1
 FLAG_FORCE_SIMT = 0x1
+FLAG_NO_SPLIT = 0x2
 
 c_int, c_void_p, c_size_t, c_float, c_double = (ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
                                                 ctypes.c_float, ctypes.c_double)

@@ -71,6 +71,8 @@ struct Plan {
   float* scal = nullptr;
   bool chunked = false;
   int nchunks = 1;
+  int* split_acc = nullptr;  // tcgen05 GEMM: accumulators and counters of the split last wave
+  int* split_cnt = nullptr;
 };
 
 static int validate(const scmp_matmul_desc* d) {
@@ -126,6 +128,17 @@ static void carve(const scmp_matmul_desc* d, Carver& c, Plan& p) {
   p.sum_a = c.take<float>(na);
   p.sum_b = c.take<float>(nb);
   p.scal = c.take<float>(8);
+  if (!(d->flags & (SCMP_FLAG_FORCE_SIMT | SCMP_FLAG_NO_SPLIT))) {
+    const int unit_d = p.chunked ? d->chunk_d : d->d;
+    const size_t bytes = gemm_tc_split_bytes(d->batch, d->n, d->m, d->d, unit_d);
+    if (bytes) {
+      char* blk = c.take<char>(bytes);
+      if (blk) {
+        p.split_acc = reinterpret_cast<int*>(blk);
+        p.split_cnt = reinterpret_cast<int*>(blk + gemm_tc_split_cnt_offset(d->batch, d->n, d->m, d->d, unit_d));
+      }
+    }
+  }
 }
 
 static QuantArgs base_quant(const scmp_matmul_desc* d, bool side_a, int q) {
@@ -237,6 +250,8 @@ int scmp_sc_matmul(const scmp_matmul_desc* d, void* workspace, size_t workspace_
   SCMP_CUDA(launch_pad_map(d->bmap, d->d, p.bmap, st), "pad bmap");
   g.unit_d = d->d;
   g.out = d->out;
+  g.split_acc = p.split_acc;
+  g.split_cnt = p.split_cnt;
   g.epi.inner = (float)(q * q) / (float)d->stoc_len;
   g.epi.fd = (float)d->d;
 

@@ -157,9 +157,50 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Persistent schedule over work items. Items 0..full-1 are whole tiles
+// 0..full-1 (all accumulation units); the remaining tiles full..tiles-1 (the
+// last, partial wave) are each split into `split` parts over contiguous ranges
+// of blocks of eight dimensions, so that the last wave keeps every SM pair
+// busy. A part stores its integer accumulator and the last part of a tile to
+// finish (a per-tile counter) adds the others' and runs the epilogue.
 struct Sched {
   int tiles, tiles_a, tiles_b, nunits, unit_d, tile_a, tile_b;
+  int full, split, nwork, nblk;
 };
+
+struct Work {
+  int tile;  // output tile
+  int part;  // K part of a split tile, -1 for a whole tile
+  int d0, d1;  // dimension range of a part
+};
+
+__device__ __forceinline__ Work work_of(const Sched& s, int w, int d) {
+  Work k;
+  if (w < s.full) {
+    k.tile = w;
+    k.part = -1;
+    k.d0 = 0;
+    k.d1 = d;
+  } else {
+    const int v = w - s.full;
+    k.tile = s.full + v / s.split;
+    k.part = v % s.split;
+    k.d0 = 8 * (int)((long long)k.part * s.nblk / s.split);
+    k.d1 = min(8 * (int)((long long)(k.part + 1) * s.nblk / s.split), d);
+  }
+  return k;
+}
+// Accumulation units of a work item and the dimension range of unit u.
+__device__ __forceinline__ int units_of(const Sched& s, const Work& k) { return k.part < 0 ? s.nunits : 1; }
+__device__ __forceinline__ void unit_range(const Sched& s, const Work& k, int u, int d, int& d0, int& d1) {
+  if (k.part < 0) {
+    d0 = u * s.unit_d;
+    d1 = min(d0 + s.unit_d, d);
+  } else {
+    d0 = k.d0;
+    d1 = k.d1;
+  }
+}
 
 __device__ __forceinline__ void tile_coords(const Sched& s, int tile, int& bh, int& a0, int& b0) {
   const int per = s.tiles_a * s.tiles_b;
@@ -253,14 +294,17 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
 #pragma unroll
   for (int k = 0; k < 8; ++k) xo[k] = (uint32_t)r * 128u + (uint32_t)((k ^ (r & 7)) << 4);
   uint32_t it = 0;
-  for (int tile = tile0; tile < sc.tiles; tile += tstep) {
+  for (int w = tile0; w < sc.nwork; w += tstep) {
+    const Work wk = work_of(sc, w, g.d);
     int bh, a0, b0;
-    tile_coords(sc, tile, bh, a0, b0);
+    tile_coords(sc, wk.tile, bh, a0, b0);
     const int row = SIDE_A ? a0 + (int)rank * C::BM + r : b0 + (int)rank * C::BNL + r;
     const bool valid = SIDE_A ? row < g.n : row < g.m;
     const int grow = bh * (SIDE_A ? g.n : g.m) + (valid ? row : 0);
-    for (int u = 0; u < sc.nunits; ++u) {
-      const int d0 = u * sc.unit_d, d1 = min(d0 + sc.unit_d, g.d);
+    const int nu = units_of(sc, wk);
+    for (int u = 0; u < nu; ++u) {
+      int d0, d1;
+      unit_range(sc, wk, u, g.d, d0, d1);
       const int nst = stages_of_unit<TLEN>(d1 - d0) * SPD;
       const int nblk = cdiv(d1 - d0, 8);
       const int blk0 = d0 >> 3;
@@ -373,6 +417,7 @@ __global__ void __launch_bounds__(Cfg<PAIR>::THREADS, 1) gemm_tc_kernel(GemmArgs
   const uint32_t drain_bar = bar_base + 8u * (2 * NST + 2);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + NST * C::STAGE_BYTES + 128);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + 136);
+  volatile int* split_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + 144);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_rank() : 0u;   // CTA rank inside the pair
@@ -420,11 +465,14 @@ __global__ void __launch_bounds__(Cfg<PAIR>::THREADS, 1) gemm_tc_kernel(GemmArgs
     // ------------------------------------------------------------ MMA issuer (leader CTA)
     if (lane == 0 && leader) {
       uint32_t it = 0, uc = 0;
-      for (int tile = tile0; tile < sc.tiles; tile += tstep) {
-        for (int u = 0; u < sc.nunits; ++u, ++uc) {
+      for (int w = tile0; w < sc.nwork; w += tstep) {
+        const Work wk = work_of(sc, w, g.d);
+        const int nu = units_of(sc, wk);
+        for (int u = 0; u < nu; ++u, ++uc) {
           if (!mbar_wait(acce_bar, (uc & 1) ^ 1, abort_flag, 4)) goto mma_done;
           tc_fence_after();
-          const int d0 = u * sc.unit_d, d1 = min(d0 + sc.unit_d, g.d);
+          int d0, d1;
+          unit_range(sc, wk, u, g.d, d0, d1);
           const int nst = stages_of_unit<TLEN>(d1 - d0) * SPD;
           for (int st = 0; st < nst; ++st, ++it) {
             const int s = it % NST;
@@ -462,10 +510,72 @@ __global__ void __launch_bounds__(Cfg<PAIR>::THREADS, 1) gemm_tc_kernel(GemmArgs
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16);
     uint32_t uc = 0;
-    for (int tile = tile0; tile < sc.tiles; tile += tstep) {
+    for (int w = tile0; w < sc.nwork; w += tstep) {
+      const Work wk = work_of(sc, w, g.d);
       int bh, a0, b0;
-      tile_coords(sc, tile, bh, a0, b0);
+      tile_coords(sc, wk.tile, bh, a0, b0);
       const int ia = a0 + (int)rank * C::BM + 32 * q + lane;
+      if (wk.part >= 0) {
+        // ---- one K part of a split tile
+        if (!mbar_wait(accf_bar, uc & 1, abort_flag, 5)) goto done;
+        ++uc;
+        tc_fence_after();
+        const int st = wk.tile - sc.full;
+        const size_t slot_ints = (size_t)C::BM * C::TILE_B;
+        const int rowq = 32 * q + lane;
+        int* mine = g.split_acc + ((size_t)(st * sc.split + wk.part) * C::NCTA + rank) * slot_ints;
+#pragma unroll 1
+        for (int cb = 0; cb < C::TILE_B / 16; ++cb) {
+          uint32_t acc[16];
+          TMEM_LD16(lane_addr + cb * 16, acc);
+          tmem_wait_ld();
+          int4* dst = reinterpret_cast<int4*>(mine + ((size_t)cb * C::BM + rowq) * 16);
+#pragma unroll
+          for (int x = 0; x < 4; ++x)
+            dst[x] = make_int4((int)acc[4 * x], (int)acc[4 * x + 1], (int)acc[4 * x + 2], (int)acc[4 * x + 3]);
+        }
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+        if (warp == C::EPI_WARP0 && lane == 0)
+          *split_flag = atomicAdd(g.split_cnt + st * C::NCTA + rank, 1) == sc.split - 1;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (*split_flag) {
+          // last part to finish: the other parts' accumulators are complete
+          __threadfence();
+#pragma unroll 1
+          for (int cb = 0; cb < C::TILE_B / 16; ++cb) {
+            uint32_t acc[16];
+            TMEM_LD16(lane_addr + cb * 16, acc);
+            tmem_wait_ld();
+            for (int p = 0; p < sc.split; ++p) {
+              if (p == wk.part) continue;
+              const int4* src = reinterpret_cast<const int4*>(
+                  g.split_acc + ((size_t)(st * sc.split + p) * C::NCTA + rank) * slot_ints +
+                  ((size_t)cb * C::BM + rowq) * 16);
+#pragma unroll
+              for (int x = 0; x < 4; ++x) {
+                const int4 v = __ldcg(src + x);
+                acc[4 * x] += (uint32_t)v.x;
+                acc[4 * x + 1] += (uint32_t)v.y;
+                acc[4 * x + 2] += (uint32_t)v.z;
+                acc[4 * x + 3] += (uint32_t)v.w;
+              }
+            }
+            if (ia < g.n) {
+              float* o = g.out + ((size_t)bh * g.n + ia) * g.m;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int ib = b0 + cb * 16 + j;
+                if (ib < g.m) o[ib] = epi_value(g.epi, (int)acc[j], bh * g.n + ia, bh * g.m + ib, bh, 0, g.n, g.m);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar, rank);
+        continue;
+      }
       const bool chunked = g.epi.kind == EPI_CHUNK;
       for (int u = 0; u < sc.nunits; ++u, ++uc) {
         if (!mbar_wait(accf_bar, uc & 1, abort_flag, 5)) goto done;
@@ -533,11 +643,11 @@ static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int sms, cudaStre
     attr = true;
   }
   if constexpr (!PAIR) {
-    const int grid = s.tiles < sms ? s.tiles : sms;
+    const int grid = s.nwork < sms ? s.nwork : sms;
     kern<<<grid, C::THREADS, C::SMEM_BYTES, st>>>(g, s);
     return cudaGetLastError();
   } else {
-    const int pairs = s.tiles < sms / 2 ? s.tiles : sms / 2;
+    const int pairs = s.nwork < sms / 2 ? s.nwork : sms / 2;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
     cfg.blockDim = dim3(C::THREADS, 1, 1);
@@ -576,20 +686,85 @@ static bool use_pair() {
   return !(e && e[0] == '1');
 }
 
-cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
-  using namespace tc;
-  const bool pair = use_pair();
+static int device_sms() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    sms = 148;
+  return sms;
+}
+
+namespace tc {
+constexpr int kMaxSplit = 8;              // K parts per tile of the last wave
+constexpr int kMinSplitBlocks = 8;        // blocks of eight dimensions per part, at least
+constexpr size_t kSplitBudget = 64u << 20;  // bytes of part accumulators, at most
+
+// Schedule of the persistent grid: `units` workers (SM pairs or SMs) take
+// whole tiles round-robin; when the tiles leave a last wave of `rem` < units
+// tiles (and d is one accumulation unit), those are split into the number of
+// K parts S that minimises the last wave's length, ceil(rem*S/units)/S of a
+// tile, within the limits above (SCMP_TC_NO_SPLIT=1 in the environment turns
+// splitting off).
+static Sched make_sched(int batch, int n, int m, int d, int unit_d, bool pair, int sms) {
   Sched s{};
   s.tile_a = pair ? Cfg<true>::TILE_A : Cfg<false>::TILE_A;
   s.tile_b = 256;
-  s.tiles_a = cdiv(g.n, s.tile_a);
-  s.tiles_b = cdiv(g.m, s.tile_b);
-  s.tiles = g.batch * s.tiles_a * s.tiles_b;
-  s.unit_d = g.unit_d > 0 ? g.unit_d : g.d;
-  s.nunits = cdiv(g.d, s.unit_d);
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  s.tiles_a = cdiv(n, s.tile_a);
+  s.tiles_b = cdiv(m, s.tile_b);
+  s.tiles = batch * s.tiles_a * s.tiles_b;
+  s.unit_d = unit_d > 0 ? unit_d : d;
+  s.nunits = cdiv(d, s.unit_d);
+  s.nblk = cdiv(d, 8);
+  s.full = s.tiles;
+  s.split = 1;
+  const int units = pair ? sms / 2 : sms;
+  const int rem = s.tiles % units;
+  const char* off = getenv("SCMP_TC_NO_SPLIT");
+  if (s.nunits == 1 && rem > 0 && !(off && off[0] == '1')) {
+    const size_t part_bytes = (size_t)(pair ? 2 : 1) * 128 * 256 * sizeof(int);
+    double best = 1.0;
+    for (int S = 2; S <= kMaxSplit && s.nblk / S >= kMinSplitBlocks; ++S) {
+      if ((size_t)rem * S * part_bytes > kSplitBudget) break;
+      const double len = (double)cdiv(rem * S, units) / S;
+      if (len < best - 1e-9) {
+        best = len;
+        s.split = S;
+      }
+    }
+    if (s.split > 1) s.full = s.tiles - rem;
+  }
+  s.nwork = s.full + (s.tiles - s.full) * s.split;
+  return s;
+}
+}  // namespace tc
+
+size_t gemm_tc_split_cnt_offset(int batch, int n, int m, int d, int unit_d) {
+  const bool pair = use_pair();
+  const tc::Sched s = tc::make_sched(batch, n, m, d, unit_d, pair, device_sms());
+  return (size_t)(s.tiles - s.full) * s.split * (pair ? 2 : 1) * 128 * 256 * sizeof(int);
+}
+
+size_t gemm_tc_split_bytes(int batch, int n, int m, int d, int unit_d) {
+  const bool pair = use_pair();
+  const tc::Sched s = tc::make_sched(batch, n, m, d, unit_d, pair, device_sms());
+  if (s.split == 1) return 0;
+  return gemm_tc_split_cnt_offset(batch, n, m, d, unit_d) + (size_t)(s.tiles - s.full) * (pair ? 2 : 1) * sizeof(int);
+}
+
+cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
+  using namespace tc;
+  const bool pair = use_pair();
+  const int sms = device_sms();
+  Sched s = make_sched(g.batch, g.n, g.m, g.d, g.unit_d, pair, sms);
+  if (s.split > 1) {
+    if (!g.split_acc || !g.split_cnt) {  // no workspace for the parts: whole tiles only
+      s.full = s.tiles;
+      s.split = 1;
+      s.nwork = s.tiles;
+    } else {
+      const cudaError_t e = cudaMemsetAsync(g.split_cnt, 0, (size_t)(s.tiles - s.full) * (pair ? 2 : 1) * sizeof(int), st);
+      if (e != cudaSuccess) return e;
+    }
+  }
   const int tlen = g.lp < 256 ? g.lp : 256;
   const int spd = g.lp / tlen;
   if (pair) {

@@ -111,6 +111,8 @@ struct GemmArgs {
   int unit_d;
   float* out;
   Epilogue epi;
+  int* split_acc;  // tcgen05 GEMM, split last wave: per-part integer accumulators
+  int* split_cnt;  //   and per-tile arrival counters (see gemm_tc_split_bytes)
 };
 
 // Host launchers (return cudaError_t of the launch).
@@ -120,5 +122,10 @@ cudaError_t launch_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, 
 cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t st);
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st);
 bool gemm_tc_supported(const GemmArgs& g);
+// Workspace of the tcgen05 GEMM's split last wave for this shape on the
+// current device (0 when the last wave is not split); the counters sit at
+// byte offset gemm_tc_split_cnt_offset of that block.
+size_t gemm_tc_split_bytes(int batch, int n, int m, int d, int unit_d);
+size_t gemm_tc_split_cnt_offset(int batch, int n, int m, int d, int unit_d);
 
 }  // namespace scmp

@@ -52,6 +52,15 @@ extern "C" int scmp_sc_matmul_noalloc(const scmp_matmul_desc* desc, void* stream
   size_t need = 0;
   int s = scmp_sc_matmul_workspace_size(desc, &need);
   if (s) return s;
+  scmp_matmul_desc whole;
+  if (need > kNoAllocScratchBytes && !(desc->flags & SCMP_FLAG_NO_SPLIT)) {
+    // without the split last wave's part accumulators the call may still fit
+    whole = *desc;
+    whole.flags |= SCMP_FLAG_NO_SPLIT;
+    desc = &whole;
+    s = scmp_sc_matmul_workspace_size(desc, &need);
+    if (s) return s;
+  }
   if (need > kNoAllocScratchBytes)
     return fail(SCMP_ERR_INVALID_ARG,
                 "sc_matmul_noalloc: this call needs " + std::to_string(need) +

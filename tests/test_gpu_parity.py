@@ -144,6 +144,35 @@ def test_tc_variants_match_simt_at_size(shape, kw, monkeypatch, env_vars):
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("shape,kw", [
+    ((1000, 5000, 512), dict(granularity="per_row", sc_prec=8)),                 # 80 tiles: 1 wave + 6
+    ((600, 300, 1000), dict(granularity="per_tensor", mode="unipolar", sc_prec=7)),  # 6 tiles, all split
+    ((9, 197, 197, 640), dict(granularity="per_head", sc_prec=8)),                 # 9 heads, one tile each
+])
+@pytest.mark.parametrize("single", ["0", "1"])
+def test_split_last_wave_matches_whole_tiles(shape, kw, single, monkeypatch, env_vars):
+    """Tiles of the last wave split over K (part accumulators summed by the
+    last part to finish) give the same bits as whole tiles."""
+    env_vars({})
+    g = torch.Generator(device=DEV).manual_seed(5)
+    if len(shape) == 4:
+        bh, n, m, d = shape
+        a = torch.randn(bh, n, d, device=DEV, generator=g)
+        b = torch.randn(bh, m, d, device=DEV, generator=g)
+    else:
+        n, m, d = shape
+        a = torch.randn(n, d, device=DEV, generator=g)
+        b = torch.randn(m, d, device=DEV, generator=g) * 0.05
+    monkeypatch.setattr(K, "_FORCE_SIMT", False)
+    monkeypatch.setenv("SCMP_TC_SINGLE", single)
+    monkeypatch.setenv("SCMP_TC_NO_SPLIT", "0")
+    y_split = sc_matmul(a, b, **kw)
+    monkeypatch.setenv("SCMP_TC_NO_SPLIT", "1")
+    y_whole = sc_matmul(a, b, **kw)
+    assert torch.equal(y_split, y_whole)
+    assert _lib.device_error() == 0
+
+
 def test_quantiser_api_vs_oracle():
     from scmp_kernels_b200 import quant as Q
     g = torch.Generator().manual_seed(3)
