@@ -213,6 +213,9 @@ int scmp_set_profile_events(void* gemm_start, void* gemm_stop);
 int scmp_device_error(int* code);
 const char* scmp_last_error(void);
 int scmp_abi_version(void);
+/* Number of CUDA kernels this library has launched in the process so far
+ * (every entry point counts its own launches). */
+unsigned long long scmp_launch_count(void);
 
 #ifdef __cplusplus
 }

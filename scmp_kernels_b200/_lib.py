@@ -46,6 +46,7 @@ class MatmulDesc(ctypes.Structure):
 # name -> (restype, argtypes); every symbol of include/scmp_b200.h
 SIGNATURES = {
     "scmp_abi_version": (c_int, []),
+    "scmp_launch_count": (ctypes.c_ulonglong, []),
     "scmp_set_profile_events": (c_int, [c_void_p, c_void_p]),
     "scmp_last_error": (ctypes.c_char_p, []),
     "scmp_device_error": (c_int, [ctypes.POINTER(c_int)]),
@@ -120,6 +121,11 @@ def device_error() -> int:
     code = c_int(0)
     check(lib().scmp_device_error(ctypes.byref(code)), "scmp_device_error")
     return code.value
+
+
+def launch_count() -> int:
+    """Kernels the library has launched in this process so far."""
+    return int(lib().scmp_launch_count())
 
 
 def stream_handle(device) -> int:

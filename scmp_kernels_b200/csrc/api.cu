@@ -18,6 +18,7 @@ __global__ void pad_map_kernel(const int32_t* __restrict__ src, int d, int32_t* 
 }
 static cudaError_t launch_pad_map(const int32_t* src, int d, int32_t* dst, cudaStream_t st) {
   pad_map_kernel<<<cdiv(d8(d) * 8, 256), 256, 0, st>>>(src, d, dst);
+  count_launch();
   return cudaGetLastError();
 }
 
@@ -166,6 +167,8 @@ using namespace scmp;
 extern "C" {
 
 int scmp_abi_version(void) { return SCMP_ABI_VERSION; }
+
+unsigned long long scmp_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int scmp_set_profile_events(void* gemm_start, void* gemm_stop) {
   g_prof_start = (cudaEvent_t)gemm_start;

@@ -4,9 +4,16 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "scmp_b200.h"
 
 namespace scmp {
+
+// Kernels launched by the library (scmp_launch_count); every launch site
+// counts itself.
+inline std::atomic<unsigned long long> g_launches{0};
+inline void count_launch(unsigned long long n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 // ---------------------------------------------------------------------------
 // IEEE float32, one rounding per operation. The intrinsics keep nvcc from

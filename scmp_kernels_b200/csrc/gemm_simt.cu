@@ -143,6 +143,7 @@ cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t st) {
   }
   dim3 grid(cdiv(g.m, TB), cdiv(g.n, TA), g.batch);
   gemm_simt_kernel<<<grid, THREADS, smem, st>>>(g);
+  count_launch();
   return cudaGetLastError();
 }
 

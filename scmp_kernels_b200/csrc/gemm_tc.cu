@@ -645,6 +645,7 @@ static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int sms, cudaStre
   if constexpr (!PAIR) {
     const int grid = s.nwork < sms ? s.nwork : sms;
     kern<<<grid, C::THREADS, C::SMEM_BYTES, st>>>(g, s);
+    count_launch();
     return cudaGetLastError();
   } else {
     const int pairs = s.nwork < sms / 2 ? s.nwork : sms / 2;
@@ -660,7 +661,9 @@ static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int sms, cudaStre
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, g, s);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, g, s);
+    count_launch();
+    return e;
   }
 }
 

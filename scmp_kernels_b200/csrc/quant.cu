@@ -303,7 +303,10 @@ __global__ void quant_rows_kernel(QuantArgs q) {
 static inline dim3 warp_grid(int rows) { return dim3(cdiv(rows, 8)); }
 
 cudaError_t launch_row_stats(const QuantArgs& q, float* stats, cudaStream_t st) {
-  if (q.rows > 0) row_stats_kernel<<<warp_grid(q.rows), 256, 0, st>>>(q, stats);
+  if (q.rows > 0) {
+    row_stats_kernel<<<warp_grid(q.rows), 256, 0, st>>>(q, stats);
+    count_launch();
+  }
   return cudaGetLastError();
 }
 
@@ -311,14 +314,18 @@ cudaError_t launch_group_params(const float* stats, int batch, int rpb, int G, i
                                 float* scale, float* zp, cudaStream_t st) {
   const int gpb = G >= rpb ? 1 : cdiv(rpb, G);
   const int ng = recipe == GP_HEAD ? batch : batch * gpb;
-  if (ng > 0) group_params_kernel<<<ng, 256, 0, st>>>(stats, rpb, recipe == GP_HEAD ? rpb : G, q,
+  if (ng > 0) {
+    group_params_kernel<<<ng, 256, 0, st>>>(stats, rpb, recipe == GP_HEAD ? rpb : G, q,
                                                        recipe, scale, zp);
+    count_launch();
+  }
   return cudaGetLastError();
 }
 
 cudaError_t launch_tensor_params(const float* sa, int ra, const float* sb, int rb, int d, int q,
                                  int unipolar, const double* ranges, float* scal, cudaStream_t st) {
   tensor_params_kernel<<<1, 1024, 0, st>>>(sa, ra, sb, rb, d, q, unipolar, ranges, scal);
+  count_launch();
   return cudaGetLastError();
 }
 
@@ -326,13 +333,13 @@ cudaError_t launch_quant_rows(int recipe, const QuantArgs& q, cudaStream_t st) {
   if (q.rows <= 0) return cudaSuccess;
   const dim3 g = warp_grid(q.rows);
   switch (recipe) {
-    case Q_TENSOR_BIP: quant_rows_kernel<Q_TENSOR_BIP><<<g, 256, 0, st>>>(q); break;
-    case Q_TENSOR_UNI: quant_rows_kernel<Q_TENSOR_UNI><<<g, 256, 0, st>>>(q); break;
-    case Q_GROUP_SYM: quant_rows_kernel<Q_GROUP_SYM><<<g, 256, 0, st>>>(q); break;
-    case Q_GROUP_ASYM: quant_rows_kernel<Q_GROUP_ASYM><<<g, 256, 0, st>>>(q); break;
-    case Q_BATCH_SYM: quant_rows_kernel<Q_BATCH_SYM><<<g, 256, 0, st>>>(q); break;
-    case Q_ROWCHUNK_BIP: quant_rows_kernel<Q_ROWCHUNK_BIP><<<g, 256, 0, st>>>(q); break;
-    case Q_HEAD_BIP: quant_rows_kernel<Q_HEAD_BIP><<<g, 256, 0, st>>>(q); break;
+    case Q_TENSOR_BIP: { quant_rows_kernel<Q_TENSOR_BIP><<<g, 256, 0, st>>>(q); count_launch(); } break;
+    case Q_TENSOR_UNI: { quant_rows_kernel<Q_TENSOR_UNI><<<g, 256, 0, st>>>(q); count_launch(); } break;
+    case Q_GROUP_SYM: { quant_rows_kernel<Q_GROUP_SYM><<<g, 256, 0, st>>>(q); count_launch(); } break;
+    case Q_GROUP_ASYM: { quant_rows_kernel<Q_GROUP_ASYM><<<g, 256, 0, st>>>(q); count_launch(); } break;
+    case Q_BATCH_SYM: { quant_rows_kernel<Q_BATCH_SYM><<<g, 256, 0, st>>>(q); count_launch(); } break;
+    case Q_ROWCHUNK_BIP: { quant_rows_kernel<Q_ROWCHUNK_BIP><<<g, 256, 0, st>>>(q); count_launch(); } break;
+    case Q_HEAD_BIP: { quant_rows_kernel<Q_HEAD_BIP><<<g, 256, 0, st>>>(q); count_launch(); } break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

@@ -117,6 +117,7 @@ int scmp_fused_quantize_bipolar(const float* x, int rows, int cols, double abs_m
   ref_bipolar_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
       x, total, rows, cols, nullptr, (float)(1.0 / scale), q, -(float)q,
       (float)rng_levels / (float)q, 0, boundary, sign);
+  count_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SCMP_OK : scmp::fail(SCMP_ERR_CUDA, cudaGetErrorString(e));
 }
@@ -129,6 +130,7 @@ int scmp_fused_quantize_bipolar_perrow(const float* x, int rows, int cols, int s
   const int q = (1 << (sc_prec - 1)) - 1;
   ref_bipolar_perrow_kernel<<<cdiv(rows, 8), 256, 0, (cudaStream_t)stream>>>(
       x, rows, cols, q, (float)rng_levels / (float)q, boundary, sign, scale_row);
+  count_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SCMP_OK : scmp::fail(SCMP_ERR_CUDA, cudaGetErrorString(e));
 }
@@ -149,6 +151,7 @@ int scmp_fused_quantize_unipolar(const float* x, int rows, int cols, double fp_m
   ref_unipolar_kernel<<<cdiv(rows, 8), 256, 0, (cudaStream_t)stream>>>(
       x, rows, cols, (float)(1.0 / scale), (float)zp, q, (float)rng_levels / (float)q, boundary,
       row_sum);
+  count_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SCMP_OK : scmp::fail(SCMP_ERR_CUDA, cudaGetErrorString(e));
 }
@@ -164,6 +167,7 @@ int scmp_fused_quant_bipolar_batched(const float* x, int bh, int rows, int cols,
   ref_bipolar_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
       x, slice, rows, cols, inv_scale, 0.f, q, -(float)(q + 1), (float)rng_levels / (float)q, 1,
       boundary, sign);
+  count_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SCMP_OK : scmp::fail(SCMP_ERR_CUDA, cudaGetErrorString(e));
 }
@@ -186,6 +190,7 @@ int scmp_grouped_symmetric_quant(const float* x, int batch, int rows, int cols, 
   const size_t total = (size_t)a.rows * cols;
   if (e == cudaSuccess) {
     ref_grouped_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(x, total, cols, q_max, 0, scale_row, nullptr, x_int, sign);
+    count_launch();
     e = cudaGetLastError();
   }
   return e == cudaSuccess ? SCMP_OK : scmp::fail(SCMP_ERR_CUDA, cudaGetErrorString(e));
@@ -207,6 +212,7 @@ int scmp_grouped_asymmetric_quant(const float* x, int rows, int cols, int group,
   const size_t total = (size_t)rows * cols;
   if (e == cudaSuccess) {
     ref_grouped_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(x, total, cols, q_max, 1, scale_row, zp_row, x_int, nullptr);
+    count_launch();
     e = cudaGetLastError();
   }
   return e == cudaSuccess ? SCMP_OK : scmp::fail(SCMP_ERR_CUDA, cudaGetErrorString(e));
@@ -247,7 +253,9 @@ int scmp_enable_matmul(const int16_t* ktab, const uint32_t* pattern, const int32
   carve_enable(n, m, d, c, &ka, &vb, &bm);
   const size_t ta = (size_t)n * d, tb = (size_t)m * d;
   encode_kernel<<<(unsigned)((ta + 255) / 256), 256, 0, st>>>(boundary_a, is_bipolar ? sign_a : nullptr, ta, n, d, ktab, amap, vcap, ka);
+  count_launch();
   encode_kernel<<<(unsigned)((tb + 255) / 256), 256, 0, st>>>(boundary_b, is_bipolar ? sign_b : nullptr, tb, m, d, nullptr, bmap, vcap, vb);
+  count_launch();
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) e = scmp::launch_pad_map(bmap, d, bm, st);
   GemmArgs g{};

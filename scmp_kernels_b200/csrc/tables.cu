@@ -54,7 +54,10 @@ cudaError_t launch_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, 
     cudaFuncSetAttribute(k_table_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     cudaFuncSetAttribute(pattern_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   }
-  if (n_ra > 0) k_table_kernel<<<n_ra, 256, sm, st>>>(ra, L, vcap, ktab);
+  if (n_ra > 0) {
+    k_table_kernel<<<n_ra, 256, sm, st>>>(ra, L, vcap, ktab);
+    count_launch();
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (n_rb > 0) {
@@ -62,6 +65,7 @@ cudaError_t launch_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, 
     const int ys = cdiv((vcap + 1) * lw, 256);
     dim3 grid(n_rb, ys < 64 ? ys : 64);
     pattern_kernel<<<grid, 256, sm, st>>>(rb, L, lp, vcap, pattern);
+    count_launch();
   }
   return cudaGetLastError();
 }
