@@ -35,16 +35,23 @@ namespace tc {
 
 constexpr int KS = 256;                    // K bytes per stage
 constexpr int PROD_A_WARPS = 4;            // 128 a rows per CTA
-constexpr int TMEM_COLS = 512;             // [0,256) accumulator, [256,512) running chunk sum
+// Tensor memory: [0,256) accumulator; [256,512) either the running chunk sum
+// (chunked path) or, with A in tensor memory, a's stages (64 columns each).
+constexpr int TMEM_COLS = 512;
+constexpr int TMEM_A_COL = 256;
 
-template <bool PAIR>
+// ATMEM (2-SM variant, one accumulation unit per tile): a's stages live in
+// tensor memory, written by the producers with tcgen05.st and read by the
+// MMA from there, so shared memory carries only b (half the traffic).
+template <bool PAIR, bool ATMEM = false>
 struct Cfg {
+  static_assert(PAIR || !ATMEM, "a in tensor memory is implemented for SM pairs");
   static constexpr int BM = 128;                          // a rows per CTA
   static constexpr int BNL = PAIR ? 128 : 256;            // b rows per CTA
   static constexpr int TILE_A = PAIR ? 256 : 128;         // a rows per tile
   static constexpr int TILE_B = 256;                      // b rows per tile (UMMA N)
-  static constexpr int NST = PAIR ? 3 : 2;                // pipeline stages
-  static constexpr int A_BYTES = BM * KS;
+  static constexpr int NST = ATMEM ? 4 : PAIR ? 3 : 2;    // pipeline stages
+  static constexpr int A_BYTES = ATMEM ? 0 : BM * KS;     // a's bytes of a smem stage
   static constexpr int B_BYTES = BNL * KS;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int A_ATOM = BM * 128;                 // one 128-byte-wide K atom
@@ -95,6 +102,16 @@ __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t
         "l"(adesc), "l"(bdesc), "r"(Cfg<false>::IDESC), "r"(acc)
         : "memory");
   }
+}
+// M=256 N=256 K=32 pair MMA with a read from tensor memory (column a_tmem of
+// lanes 0..127 in both CTAs) and b from shared memory.
+__device__ __forceinline__ void mma_i8_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(Cfg<true>::IDESC), "r"(acc)
+      : "memory");
 }
 // Arrive on `bar` (same offset) in every CTA of the tile once all MMAs issued
 // so far by this thread have completed.
@@ -277,11 +294,13 @@ __device__ __forceinline__ int stages_of_unit(int len) {
 // the loads are in flight while the producer waits for its shared-memory
 // slot. Stages are not unrolled (the instruction cache holds both sides'
 // loops); the chunks of a stage are. Returns false after an abort.
-template <bool SIDE_A, int TLEN, int SPD, bool PAIR>
+// With ATMEM, side a writes its row's 64 columns of each stage to tensor
+// memory at tmem_a (this thread's lane, first stage column) instead.
+template <bool SIDE_A, int TLEN, int SPD, bool PAIR, bool ATMEM>
 __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint32_t sbase, uint32_t bar_base,
                                         volatile int* abort_flag, uint32_t rank, int tile0, int tstep, int r,
-                                        int lane) {
-  using C = Cfg<PAIR>;
+                                        int lane, uint32_t tmem_a) {
+  using C = Cfg<PAIR, ATMEM>;
   constexpr int NST = C::NST;
   constexpr int DPS = TLEN < 256 ? 256 / TLEN : 1;
   constexpr int NSPB = SPB<TLEN, SPD>();
@@ -343,44 +362,75 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
             return false;
           const uint32_t stage = sbase + s * C::STAGE_BYTES + (SIDE_A ? 0 : C::A_BYTES);
           const int tbase = (j % SPD) * TLEN;
+          if constexpr (SIDE_A && ATMEM) {
+            // stage s of a in tensor memory: K bytes 4x..4x+3 in column x of
+            // this row's lane, 16 columns (four 16-byte chunks) per store;
+            // the MMAs that read the slot before have completed (empty barrier)
+            tc_fence_after();
+            constexpr int CPD = TLEN / 16;  // chunks per dimension piece
+            uint32_t fillv[DPS];
+            int shv[DPS];
 #pragma unroll
-          for (int dl = 0; dl < DPS; ++dl) {
-            const int e = (j / SPD) * DPS + dl;  // dimension inside the block
-            const int kv = (dbase + e < d1) ? kv_at(kv_cur, e) : 0;
-            const int mag = kv < 0 ? -kv : kv;
-            if (SIDE_A) {
-              // word x of the piece holds positions 4x..4x+3: its low
-              // clamp(mag - tbase - 4x, 0, 4) bytes are `fill`, i.e. the top
-              // bytes of (0:fill) << max(8*(mag - tbase) - 32x, 0), clamped at 32
-              const uint32_t fill = kv < 0 ? 0xFFFFFFFFu : 0x01010101u;
-              const int sh = 8 * (mag - tbase);
+            for (int dl = 0; dl < DPS; ++dl) {
+              const int e = (j / SPD) * DPS + dl;
+              const int kv = (dbase + e < d1) ? kv_at(kv_cur, e) : 0;
+              fillv[dl] = kv < 0 ? 0xFFFFFFFFu : 0x01010101u;
+              shv[dl] = 8 * ((kv < 0 ? -kv : kv) - tbase);
+            }
 #pragma unroll
-              for (int c = 0; c < TLEN / 16; ++c) {
-                uint32_t w[4];
+            for (int grp = 0; grp < 4; ++grp) {
+              uint32_t wv[16];
+#pragma unroll
+              for (int x = 0; x < 4; ++x) {
+                const int kc = 4 * grp + x, dl = kc / CPD, c = kc % CPD;
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                  w[q] = __funnelshift_lc(fill, 0u, (uint32_t)max(sh - 32 * (4 * c + q), 0));
-                const int kc = dl * (TLEN / 16) + c;
-                st_shared_v4(stage + (kc >> 3) * C::A_ATOM + xo[kc & 7], w[0], w[1], w[2], w[3]);
+                  wv[4 * x + q] = __funnelshift_lc(fillv[dl], 0u, (uint32_t)max(shv[dl] - 32 * (4 * c + q), 0));
               }
-            } else {
-              // sliced stream words: chunk c's four words are the bytes'
-              // bit 0 of (word >> (4*(c&1) + q)), negated for v < 0
-              const uint32_t mult = kv < 0 ? 0xFFu : 1u;
+              TMEM_ST16(tmem_a + (uint32_t)(s * 64 + 16 * grp), wv);
+            }
+            tmem_wait_st();
+            tc_fence_before();  // the stores precede the arrive for the MMA
+          } else {
 #pragma unroll
-              for (int c = 0; c < TLEN / 16; ++c) {
-                const uint32_t sw = pw[dl * (TLEN / 32) + (c >> 1)];
-                uint32_t w[4];
+            for (int dl = 0; dl < DPS; ++dl) {
+              const int e = (j / SPD) * DPS + dl;  // dimension inside the block
+              const int kv = (dbase + e < d1) ? kv_at(kv_cur, e) : 0;
+              const int mag = kv < 0 ? -kv : kv;
+              if (SIDE_A) {
+                // word x of the piece holds positions 4x..4x+3: its low
+                // clamp(mag - tbase - 4x, 0, 4) bytes are `fill`, i.e. the top
+                // bytes of (0:fill) << max(8*(mag - tbase) - 32x, 0), clamped at 32
+                const uint32_t fill = kv < 0 ? 0xFFFFFFFFu : 0x01010101u;
+                const int sh = 8 * (mag - tbase);
 #pragma unroll
-                for (int q = 0; q < 4; ++q) w[q] = ((sw >> (4 * (c & 1) + q)) & 0x01010101u) * mult;
-                const int kc = dl * (TLEN / 16) + c;
-                st_shared_v4(stage + (kc >> 3) * C::B_ATOM + xo[kc & 7], w[0], w[1], w[2], w[3]);
+                for (int c = 0; c < TLEN / 16; ++c) {
+                  uint32_t w[4];
+#pragma unroll
+                  for (int q = 0; q < 4; ++q)
+                    w[q] = __funnelshift_lc(fill, 0u, (uint32_t)max(sh - 32 * (4 * c + q), 0));
+                  const int kc = dl * (TLEN / 16) + c;
+                  st_shared_v4(stage + (kc >> 3) * C::A_ATOM + xo[kc & 7], w[0], w[1], w[2], w[3]);
+                }
+              } else {
+                // sliced stream words: chunk c's four words are the bytes'
+                // bit 0 of (word >> (4*(c&1) + q)), negated for v < 0
+                const uint32_t mult = kv < 0 ? 0xFFu : 1u;
+#pragma unroll
+                for (int c = 0; c < TLEN / 16; ++c) {
+                  const uint32_t sw = pw[dl * (TLEN / 32) + (c >> 1)];
+                  uint32_t w[4];
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) w[q] = ((sw >> (4 * (c & 1) + q)) & 0x01010101u) * mult;
+                  const int kc = dl * (TLEN / 16) + c;
+                  st_shared_v4(stage + (kc >> 3) * C::B_ATOM + xo[kc & 7], w[0], w[1], w[2], w[3]);
+                }
               }
             }
+            // every lane's stores become visible to the tensor core, then one
+            // lane signals the tile's leader CTA for the whole warp
+            fence_proxy_async();
           }
-          // every lane's stores become visible to the tensor core, then one
-          // lane signals the tile's leader CTA for the whole warp
-          fence_proxy_async();
           __syncwarp();
           if (lane == 0) mbar_arrive_leader<PAIR>(bar_base + 8u * s, rank);
           ++it;
@@ -401,9 +451,9 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
 
 // TLEN: padded stream length lp when lp <= 256 (256/lp dimensions per stage),
 // or 256 when lp = 256*SPD (SPD stages per dimension, SPD = 1 or 2).
-template <int TLEN, int SPD, bool PAIR>
-__global__ void __launch_bounds__(Cfg<PAIR>::THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched sc) {
-  using C = Cfg<PAIR>;
+template <int TLEN, int SPD, bool PAIR, bool ATMEM>
+__global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched sc) {
+  using C = Cfg<PAIR, ATMEM>;
   constexpr int NST = C::NST;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -456,11 +506,13 @@ __global__ void __launch_bounds__(Cfg<PAIR>::THREADS, 1) gemm_tc_kernel(GemmArgs
 
   if (warp < C::PROD_WARPS) {
     // ------------------------------------------------------------ producers
+    // a's warp w writes tensor-memory lanes 32w..32w+31 (its rows)
     if (warp < PROD_A_WARPS)
-      produce<true, TLEN, SPD, PAIR>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep, threadIdx.x, lane);
+      produce<true, TLEN, SPD, PAIR, ATMEM>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep, threadIdx.x,
+                                            lane, tmem + ((uint32_t)(32 * warp) << 16) + TMEM_A_COL);
     else
-      produce<false, TLEN, SPD, PAIR>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep,
-                                      threadIdx.x - PROD_A_WARPS * 32, lane);
+      produce<false, TLEN, SPD, PAIR, ATMEM>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep,
+                                             threadIdx.x - PROD_A_WARPS * 32, lane, 0u);
   } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer (leader CTA)
     if (lane == 0 && leader) {
@@ -482,8 +534,13 @@ __global__ void __launch_bounds__(Cfg<PAIR>::THREADS, 1) gemm_tc_kernel(GemmArgs
 #pragma unroll
             for (int kk = 0; kk < KS / 32; ++kk) {
               const uint32_t off = (kk & 3) * 32;
-              mma_i8<PAIR>(tmem, smem_desc(a_base + (kk >> 2) * C::A_ATOM + off),
-                           smem_desc(b_base + (kk >> 2) * C::B_ATOM + off), (st > 0 || kk > 0) ? 1u : 0u);
+              const uint32_t acc = (st > 0 || kk > 0) ? 1u : 0u;
+              if constexpr (ATMEM)
+                mma_i8_ts(tmem, tmem + TMEM_A_COL + s * 64 + kk * 8, smem_desc(b_base + (kk >> 2) * C::B_ATOM + off),
+                          acc);
+              else
+                mma_i8<PAIR>(tmem, smem_desc(a_base + (kk >> 2) * C::A_ATOM + off),
+                             smem_desc(b_base + (kk >> 2) * C::B_ATOM + off), acc);
             }
             mma_commit<PAIR>(empty_bar(s));
           }
@@ -632,11 +689,11 @@ done:
   }
 }
 
-template <int TLEN, int SPD, bool PAIR>
+template <int TLEN, int SPD, bool PAIR, bool ATMEM = false>
 static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int sms, cudaStream_t st) {
-  using C = Cfg<PAIR>;
+  using C = Cfg<PAIR, ATMEM>;
   static bool attr = false;
-  auto kern = gemm_tc_kernel<TLEN, SPD, PAIR>;
+  auto kern = gemm_tc_kernel<TLEN, SPD, PAIR, ATMEM>;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
@@ -770,6 +827,18 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
   }
   const int tlen = g.lp < 256 ? g.lp : 256;
   const int spd = g.lp / tlen;
+  // a in tensor memory needs the running-sum columns free: one accumulation
+  // unit per tile (SCMP_TC_ASMEM=1 keeps a in shared memory)
+  const char* asmem = getenv("SCMP_TC_ASMEM");
+  if (pair && s.nunits == 1 && !(asmem && asmem[0] == '1')) {
+    switch (tlen) {
+      case 32: return launch_t<32, 1, true, true>(g, s, sms, st);
+      case 64: return launch_t<64, 1, true, true>(g, s, sms, st);
+      case 128: return launch_t<128, 1, true, true>(g, s, sms, st);
+      default:
+        return spd == 2 ? launch_t<256, 2, true, true>(g, s, sms, st) : launch_t<256, 1, true, true>(g, s, sms, st);
+    }
+  }
   if (pair) {
     switch (tlen) {
       case 32: return launch_t<32, 1, true>(g, s, sms, st);

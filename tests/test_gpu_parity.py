@@ -28,10 +28,13 @@ from scmp_kernels_b200.sc import kernels as K  # noqa: E402
 DEV = "cuda:0"
 
 
-@pytest.fixture(params=["tc2", "tc1", "simt"])
+@pytest.fixture(params=["tc2", "tc2smem", "tc1", "simt"])
 def impl(request, monkeypatch):
-    """tc2: tcgen05 on SM pairs (default); tc1: tcgen05 on single SMs; simt: CUDA cores."""
+    """tc2: tcgen05 on SM pairs, a in tensor memory where the path allows
+    (default); tc2smem: SM pairs with a in shared memory; tc1: tcgen05 on
+    single SMs; simt: CUDA cores."""
     monkeypatch.setattr(K, "_FORCE_SIMT", request.param == "simt")
+    monkeypatch.setenv("SCMP_TC_ASMEM", "1" if request.param == "tc2smem" else "0")
     if request.param == "tc1":
         monkeypatch.setenv("SCMP_TC_SINGLE", "1")
     else:
@@ -136,11 +139,15 @@ def test_tc_variants_match_simt_at_size(shape, kw, monkeypatch, env_vars):
     a = torch.randn(n, d, device=DEV, generator=g)
     b = torch.randn(m, d, device=DEV, generator=g) * 0.02
     outs = []
-    for simt, single in ((True, "0"), (False, "0"), (False, "1")):
+    # CUDA cores; SM pairs (a in tensor memory unless chunked); SM pairs with a
+    # in shared memory; single SMs
+    for simt, single, asmem in ((True, "0", "0"), (False, "0", "0"), (False, "0", "1"), (False, "1", "0")):
         monkeypatch.setattr(K, "_FORCE_SIMT", simt)
         monkeypatch.setenv("SCMP_TC_SINGLE", single)
+        monkeypatch.setenv("SCMP_TC_ASMEM", asmem)
         outs.append(sc_matmul(a, b, **kw))
-    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    for i, o in enumerate(outs[1:], 1):
+        assert torch.equal(outs[0], o), f"variant {i} differs from the CUDA-core GEMM"
     assert _lib.device_error() == 0
 
 
