@@ -38,6 +38,13 @@ WORKLOADS = {
 }
 
 
+# DRAM bytes of one GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum)
+# from an ncu capture of the 2048-row case of the config-2 recipe (539.2 MB,
+# profiles/gemm_tc_pair_tmemA_2048x11008x4096.md), scaled to the 4096 rows of
+# the full workload: the a rows and the bands of a that re-read b both double.
+GEMM_TRAFFIC_BYTES = {"config2": 2 * 539.2e6}
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -340,7 +347,9 @@ def main():
             "gpu_launches": launches,
             "gemm_ms_per_step": gemm_ms,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS (int8)",
-                         "frac": achieved / int8_peak, "traffic": None,
+                         "frac": achieved / int8_peak,
+                         "traffic": (GEMM_TRAFFIC_BYTES.get(args.workload) if shape is None and world == 1
+                                     else None),
                          "peak_source": f"2 x bf16_tflops of {src} peaks (int8 dense = 2 x bf16 dense)"},
             "clocks": clocks,
             "e2e": e2e,
