@@ -358,6 +358,7 @@ def main():
             line["cpu_baseline"] = cpu_baseline(args.workload)
         print(json.dumps(line), flush=True)
     if world > 1:
+        SD.release_peer_buffers()
         dist.barrier()
         dist.destroy_process_group()
 

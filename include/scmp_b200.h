@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define SCMP_ABI_VERSION 1
+#define SCMP_ABI_VERSION 2
 
 enum scmp_status {
   SCMP_OK = 0,
@@ -120,7 +120,33 @@ typedef struct scmp_matmul_desc {
                                   device; the max_fp_* / min_fp_* arguments of
                                   _sc_matmul_per_tensor (kernels.py:1053-1066), e.g.
                                   global ranges when b is sharded over devices       */
+  /* Result written to several buffers, e.g. this rank's column block into every
+   * rank's full output (an all-gather fused into the GEMM's epilogue; no
+   * reference counterpart). When n_out_peers > 0, `out` is ignored and element
+   * (h, i, j) of the (batch, n, m) result is stored at
+   *   out_peers[k][out_offset + (h*n + i) * out_ld + j]   for k < n_out_peers,
+   * out_peers being a HOST array of device pointers (this device's memory or
+   * peers' memory mapped with scmp_peer_open). */
+  float* const* out_peers;
+  int n_out_peers;         /* 0 .. SCMP_MAX_OUT_PEERS                              */
+  int out_ld;              /* row stride of the destinations, >= m                */
+  long long out_offset;    /* element offset of (0, 0, 0) in every destination    */
 } scmp_matmul_desc;
+
+#define SCMP_MAX_OUT_PEERS 8
+
+/*
+ * Device buffers shared between the processes of one node (CUDA IPC), the
+ * destinations of a fused all-gather. scmp_peer_alloc allocates `bytes` on
+ * the current device and returns the pointer and a 64-byte handle that other
+ * processes pass to scmp_peer_open to map the same memory (peer access
+ * enabled); scmp_peer_close unmaps a mapped buffer, scmp_peer_free frees an
+ * allocated one.
+ */
+int scmp_peer_alloc(size_t bytes, void** ptr, void* handle64);
+int scmp_peer_open(const void* handle64, void** ptr);
+int scmp_peer_close(void* ptr);
+int scmp_peer_free(void* ptr);
 
 /* Bytes of device workspace scmp_sc_matmul needs for `desc` (host-only call). */
 int scmp_sc_matmul_workspace_size(const scmp_matmul_desc* desc, size_t* bytes);

@@ -26,6 +26,8 @@ PER_TENSOR, PER_ROW, PER_HEAD = 0, 1, 2
 BIPOLAR, UNIPOLAR = 0, 1
 FLAG_FORCE_SIMT = 0x1
 FLAG_NO_SPLIT = 0x2
+ABI_VERSION = 2
+MAX_OUT_PEERS = 8
 
 c_int, c_void_p, c_size_t, c_float, c_double = (ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
                                                 ctypes.c_float, ctypes.c_double)
@@ -40,6 +42,7 @@ class MatmulDesc(ctypes.Structure):
         ("a", c_void_p), ("b", c_void_p), ("smooth_scales", c_void_p), ("out", c_void_p),
         ("ktab", c_void_p), ("pattern", c_void_p), ("amap", c_void_p), ("bmap", c_void_p),
         ("vcap", c_int), ("lp", c_int), ("flags", c_int), ("tensor_ranges", c_void_p),
+        ("out_peers", c_void_p), ("n_out_peers", c_int), ("out_ld", c_int), ("out_offset", ctypes.c_longlong),
     ]
 
 
@@ -52,6 +55,10 @@ SIGNATURES = {
     "scmp_device_error": (c_int, [ctypes.POINTER(c_int)]),
     "scmp_build_tables": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                   c_void_p, c_void_p]),
+    "scmp_peer_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p), c_void_p]),
+    "scmp_peer_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "scmp_peer_close": (c_int, [c_void_p]),
+    "scmp_peer_free": (c_int, [c_void_p]),
     "scmp_sc_matmul_workspace_size": (c_int, [ctypes.POINTER(MatmulDesc), ctypes.POINTER(c_size_t)]),
     "scmp_sc_matmul": (c_int, [ctypes.POINTER(MatmulDesc), c_void_p, c_size_t, c_void_p]),
     "scmp_sc_matmul_noalloc": (c_int, [ctypes.POINTER(MatmulDesc), c_void_p]),
@@ -93,7 +100,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.scmp_abi_version() != 1:
+        if lib.scmp_abi_version() != ABI_VERSION:
             raise RuntimeError("scmp_kernels_b200: ABI version mismatch; rebuild the library")
         _lib = lib
         return lib
@@ -121,6 +128,20 @@ def device_error() -> int:
     code = c_int(0)
     check(lib().scmp_device_error(ctypes.byref(code)), "scmp_device_error")
     return code.value
+
+
+def peer_alloc(nbytes: int) -> tuple[int, bytes]:
+    """Device buffer on the current device and its 64-byte IPC handle."""
+    ptr, handle = c_void_p(), ctypes.create_string_buffer(64)
+    check(lib().scmp_peer_alloc(nbytes, ctypes.byref(ptr), handle), "scmp_peer_alloc")
+    return int(ptr.value), handle.raw
+
+
+def peer_open(handle: bytes) -> int:
+    """Map another process's scmp_peer_alloc buffer into this one."""
+    ptr = c_void_p()
+    check(lib().scmp_peer_open(ctypes.create_string_buffer(handle, 64), ctypes.byref(ptr)), "scmp_peer_open")
+    return int(ptr.value)
 
 
 def launch_count() -> int:

@@ -1,5 +1,6 @@
 // extern "C" entry points declared in include/scmp_b200.h.
 #include <stdio.h>
+#include <string.h>
 
 #include <string>
 
@@ -97,6 +98,10 @@ static int validate(const scmp_matmul_desc* d) {
     return fail(SCMP_ERR_INVALID_ARG, "sc_matmul: bad shape (batch >= 1, n, m >= 0, d >= 1)");
   if (d->group_a < 1 || d->group_b < 1)
     return fail(SCMP_ERR_INVALID_ARG, "sc_matmul: group sizes must be >= 1");
+  if (d->n_out_peers < 0 || d->n_out_peers > SCMP_MAX_OUT_PEERS)
+    return fail(SCMP_ERR_INVALID_ARG, "sc_matmul: n_out_peers must be in [0, SCMP_MAX_OUT_PEERS]");
+  if (d->n_out_peers > 0 && (d->out_ld < d->m || d->out_offset < 0 || !d->out_peers))
+    return fail(SCMP_ERR_INVALID_ARG, "sc_matmul: out_peers needs out_ld >= m, out_offset >= 0 and the pointer array");
   if (d->granularity == SCMP_PER_ROW && d->batch > 1 && d->mode == SCMP_BIPOLAR) {
     auto ok = [&](int g, int rows) { return g == 1 || g >= rows; };
     if (!ok(d->group_a, d->n) || !ok(d->group_b, d->m))
@@ -204,6 +209,40 @@ int scmp_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, int n_rb, 
   return SCMP_OK;
 }
 
+int scmp_peer_alloc(size_t bytes, void** ptr, void* handle64) {
+  if (!ptr || !handle64 || bytes == 0) return fail(SCMP_ERR_INVALID_ARG, "peer_alloc: bad arguments");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+  void* p = nullptr;
+  SCMP_CUDA(cudaMalloc(&p, bytes), "peer_alloc: cudaMalloc");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "peer_alloc: cudaIpcGetMemHandle");
+  }
+  memcpy(handle64, &h, sizeof h);
+  *ptr = p;
+  return SCMP_OK;
+}
+
+int scmp_peer_open(const void* handle64, void** ptr) {
+  if (!ptr || !handle64) return fail(SCMP_ERR_INVALID_ARG, "peer_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof h);
+  SCMP_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "peer_open: cudaIpcOpenMemHandle");
+  return SCMP_OK;
+}
+
+int scmp_peer_close(void* ptr) {
+  SCMP_CUDA(cudaIpcCloseMemHandle(ptr), "peer_close");
+  return SCMP_OK;
+}
+
+int scmp_peer_free(void* ptr) {
+  SCMP_CUDA(cudaFree(ptr), "peer_free");
+  return SCMP_OK;
+}
+
 int scmp_sc_matmul_workspace_size(const scmp_matmul_desc* desc, size_t* bytes) {
   int s = validate(desc);
   if (s) return s;
@@ -220,8 +259,10 @@ int scmp_sc_matmul(const scmp_matmul_desc* d, void* workspace, size_t workspace_
   int s = validate(d);
   if (s) return s;
   if (d->n == 0 || d->m == 0) return SCMP_OK;
-  if (!d->a || !d->b || !d->out || !d->ktab || !d->pattern || !d->amap || !d->bmap)
+  if (!d->a || !d->b || (!d->out && d->n_out_peers == 0) || !d->ktab || !d->pattern || !d->amap || !d->bmap)
     return fail(SCMP_ERR_INVALID_ARG, "sc_matmul: null operand, output or table pointer");
+  for (int k = 0; k < d->n_out_peers; ++k)
+    if (!d->out_peers[k]) return fail(SCMP_ERR_INVALID_ARG, "sc_matmul: null out_peers entry");
   Carver c;
   Plan p;
   carve(d, c, p);
@@ -252,7 +293,19 @@ int scmp_sc_matmul(const scmp_matmul_desc* d, void* workspace, size_t workspace_
   g.bmap = p.bmap;
   SCMP_CUDA(launch_pad_map(d->bmap, d->d, p.bmap, st), "pad bmap");
   g.unit_d = d->d;
-  g.out = d->out;
+  if (d->n_out_peers > 0) {
+    for (int k = 0; k < d->n_out_peers; ++k) g.outs[k] = d->out_peers[k];
+    g.nouts = d->n_out_peers;
+    g.out_off = d->out_offset;
+    g.out_ld = d->out_ld;
+  } else {
+    g.outs[0] = d->out;
+    g.nouts = 1;
+    g.out_off = 0;
+    g.out_ld = d->m;
+  }
+  g.out_vec = g.out_off % 4 == 0 && g.out_ld % 4 == 0;
+  for (int k = 0; k < g.nouts; ++k) g.out_vec &= (reinterpret_cast<uintptr_t>(g.outs[k]) & 15) == 0;
   g.split_acc = p.split_acc;
   g.split_cnt = p.split_cnt;
   g.epi.inner = (float)(q * q) / (float)d->stoc_len;

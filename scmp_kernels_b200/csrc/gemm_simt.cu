@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(GemmArgs g) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int ib = b0 + tx * 4 + j;
-      if (ia < g.n && ib < g.m) g.out[((size_t)bh * g.n + ia) * g.m + ib] = run[i][j];
+      if (ia < g.n && ib < g.m) store_out(g, bh, ia, ib, run[i][j]);
     }
   }
 }

@@ -62,7 +62,9 @@ struct Cfg {
   static constexpr int EPI_WARP0 = MMA_WARP + 1;
   static constexpr int NWARPS = EPI_WARP0 + 4;
   static constexpr int THREADS = NWARPS * 32;
-  static constexpr int SMEM_BYTES = NST * STAGE_BYTES + 1024 + 256;
+  // epilogue staging: 4 warps x 32 rows x 32 result columns (float32)
+  static constexpr int STG_BYTES = 4 * 32 * 32 * 4;
+  static constexpr int SMEM_BYTES = NST * STAGE_BYTES + STG_BYTES + 1024 + 256;
   static constexpr int NCTA = PAIR ? 2 : 1;
   // kind::i8, D = s32, A = B = s8, K-major; N = 256, M = 128 per SM
   static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TILE_B >> 3) << 17) |
@@ -159,17 +161,17 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
   asm volatile(                                                                                    \
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14," \
       "%15}, [%16];"                                                                               \
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),       \
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),   \
-        "=r"(r[14]), "=r"(r[15])                                                                   \
+      : "=r"((r)[0]), "=r"((r)[1]), "=r"((r)[2]), "=r"((r)[3]), "=r"((r)[4]), "=r"((r)[5]),      \
+        "=r"((r)[6]), "=r"((r)[7]), "=r"((r)[8]), "=r"((r)[9]), "=r"((r)[10]), "=r"((r)[11]),      \
+        "=r"((r)[12]), "=r"((r)[13]), "=r"((r)[14]), "=r"((r)[15])                                 \
       : "r"(taddr))
 #define TMEM_ST16(taddr, r)                                                                        \
   asm volatile(                                                                                    \
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13," \
       "%14,%15,%16};" ::"r"(taddr),                                                                \
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),     \
-      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),           \
-      "r"(r[15]))
+      "r"((r)[0]), "r"((r)[1]), "r"((r)[2]), "r"((r)[3]), "r"((r)[4]), "r"((r)[5]), "r"((r)[6]),  \
+      "r"((r)[7]), "r"((r)[8]), "r"((r)[9]), "r"((r)[10]), "r"((r)[11]), "r"((r)[12]),             \
+      "r"((r)[13]), "r"((r)[14]), "r"((r)[15]))
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -180,6 +182,53 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 // of blocks of eight dimensions, so that the last wave keeps every SM pair
 // busy. A part stores its integer accumulator and the last part of a tile to
 // finish (a per-tile counter) adds the others' and runs the epilogue.
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// Result rows ia0 .. ia0+31 (lane l holds row ia0 + l in v), columns
+// ib0 .. ib0+31, to every destination of the result (the columns < m of the
+// rows < n). The warp transposes through its 4 KB staging area `stg` so that
+// each store instruction writes four 128-byte row segments (16 bytes per
+// lane) instead of 32 scattered words: full lines for local HBM and for a
+// peer's memory over NVLink alike. Chunks are XOR-swizzled by row, so both
+// the row-wise writes and the segment-wise reads are free of bank conflicts.
+__device__ __forceinline__ void store_rows32(const GemmArgs& g, uint32_t stg, int bh, int ia0, int ib0,
+                                             const uint32_t (&v)[32], int lane) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    st_shared_v4(stg + lane * 128 + ((k ^ (lane & 7)) << 4), v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+  __syncwarp();
+  const int c = lane & 7;  // 16-byte chunk of the row segment this lane writes
+  const int ib = ib0 + 4 * c;
+#pragma unroll 1
+  for (int rr = 0; rr < 8; ++rr) {
+    const int r = 4 * rr + (lane >> 3);
+    const uint4 x = ld_shared_v4(stg + r * 128 + ((c ^ (r & 7)) << 4));
+    const int ia = ia0 + r;
+    if (ia < g.n && ib < g.m) {
+      const long long idx = g.out_off + ((long long)bh * g.n + ia) * g.out_ld + ib;
+      const bool whole = g.out_vec && ib + 3 < g.m;
+#pragma unroll 1
+      for (int k = 0; k < g.nouts; ++k) {
+        float* o = g.outs[k] + idx;
+        if (whole) {
+          *reinterpret_cast<uint4*>(o) = x;
+        } else {
+          o[0] = __uint_as_float(x.x);
+          if (ib + 1 < g.m) o[1] = __uint_as_float(x.y);
+          if (ib + 2 < g.m) o[2] = __uint_as_float(x.z);
+          if (ib + 3 < g.m) o[3] = __uint_as_float(x.w);
+        }
+      }
+    }
+  }
+  __syncwarp();
+}
+
 struct Sched {
   int tiles, tiles_a, tiles_b, nunits, unit_d, tile_a, tile_b;
   int full, split, nwork, nblk;
@@ -459,15 +508,16 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sbase = (raw + 1023u) & ~1023u;  // SW128 tiles need 1024-B alignment; the
   uint8_t* gbase = smem_raw + (sbase - raw);      // offset is the same in both CTAs of a pair
-  const uint32_t bar_base = sbase + NST * C::STAGE_BYTES;
+  const uint32_t stg_base = sbase + NST * C::STAGE_BYTES;   // epilogue staging
+  const uint32_t bar_base = stg_base + C::STG_BYTES;
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (NST + s); };
   const uint32_t accf_bar = bar_base + 8u * (2 * NST);
   const uint32_t acce_bar = bar_base + 8u * (2 * NST + 1);
   const uint32_t drain_bar = bar_base + 8u * (2 * NST + 2);
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + NST * C::STAGE_BYTES + 128);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + 136);
-  volatile int* split_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + 144);
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + 128);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + 136);
+  volatile int* split_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + 144);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_rank() : 0u;   // CTA rank inside the pair
@@ -566,6 +616,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16);
+    const uint32_t stg = stg_base + (uint32_t)q * (32 * 32 * 4);  // this warp's staging area
     uint32_t uc = 0;
     for (int w = tile0; w < sc.nwork; w += tstep) {
       const Work wk = work_of(sc, w, g.d);
@@ -600,32 +651,38 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
           // last part to finish: the other parts' accumulators are complete
           __threadfence();
 #pragma unroll 1
-          for (int cb = 0; cb < C::TILE_B / 16; ++cb) {
-            uint32_t acc[16];
-            TMEM_LD16(lane_addr + cb * 16, acc);
-            tmem_wait_ld();
-            for (int p = 0; p < sc.split; ++p) {
-              if (p == wk.part) continue;
-              const int4* src = reinterpret_cast<const int4*>(
-                  g.split_acc + ((size_t)(st * sc.split + p) * C::NCTA + rank) * slot_ints +
-                  ((size_t)cb * C::BM + rowq) * 16);
+          for (int cp = 0; cp < C::TILE_B / 32; ++cp) {
+            uint32_t fin[32];
 #pragma unroll
-              for (int x = 0; x < 4; ++x) {
-                const int4 v = __ldcg(src + x);
-                acc[4 * x] += (uint32_t)v.x;
-                acc[4 * x + 1] += (uint32_t)v.y;
-                acc[4 * x + 2] += (uint32_t)v.z;
-                acc[4 * x + 3] += (uint32_t)v.w;
+            for (int h = 0; h < 2; ++h) {
+              const int cb = 2 * cp + h;
+              uint32_t acc[16];
+              TMEM_LD16(lane_addr + cb * 16, acc);
+              tmem_wait_ld();
+              for (int p = 0; p < sc.split; ++p) {
+                if (p == wk.part) continue;
+                const int4* src = reinterpret_cast<const int4*>(
+                    g.split_acc + ((size_t)(st * sc.split + p) * C::NCTA + rank) * slot_ints +
+                    ((size_t)cb * C::BM + rowq) * 16);
+#pragma unroll
+                for (int x = 0; x < 4; ++x) {
+                  const int4 v = __ldcg(src + x);
+                  acc[4 * x] += (uint32_t)v.x;
+                  acc[4 * x + 1] += (uint32_t)v.y;
+                  acc[4 * x + 2] += (uint32_t)v.z;
+                  acc[4 * x + 3] += (uint32_t)v.w;
+                }
               }
-            }
-            if (ia < g.n) {
-              float* o = g.out + ((size_t)bh * g.n + ia) * g.m;
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
                 const int ib = b0 + cb * 16 + j;
-                if (ib < g.m) o[ib] = epi_value(g.epi, (int)acc[j], bh * g.n + ia, bh * g.m + ib, bh, 0, g.n, g.m);
+                fin[16 * h + j] =
+                    (ia < g.n && ib < g.m)
+                        ? __float_as_uint(epi_value(g.epi, (int)acc[j], bh * g.n + ia, bh * g.m + ib, bh, 0, g.n, g.m))
+                        : 0u;
               }
             }
+            store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, fin, lane);
           }
         }
         tc_fence_before();
@@ -639,32 +696,30 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
         tc_fence_after();
         const bool last = u == sc.nunits - 1;
 #pragma unroll 1
-        for (int cb = 0; cb < C::TILE_B / 16; ++cb) {
-          uint32_t acc[16], run[16];
-          TMEM_LD16(lane_addr + cb * 16, acc);
-          if (chunked && u > 0) TMEM_LD16(lane_addr + 256 + cb * 16, run);
-          tmem_wait_ld();
+        for (int cp = 0; cp < C::TILE_B / 32; ++cp) {
+          uint32_t fin[32];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int ib = b0 + cb * 16 + j;
-            float v = 0.f;
-            if (ia < g.n && ib < g.m)
-              v = epi_value(g.epi, (int)acc[j], bh * g.n + ia, bh * g.m + ib, bh, u, g.n, g.m);
-            if (chunked) v = fadd(u > 0 ? __uint_as_float(run[j]) : 0.f, v);
-            run[j] = __float_as_uint(v);
-          }
-          if (!chunked || last) {
-            if (ia < g.n) {
-              float* o = g.out + ((size_t)bh * g.n + ia) * g.m;
+          for (int h = 0; h < 2; ++h) {
+            const int cb = 2 * cp + h;
+            uint32_t acc[16], run[16];
+            TMEM_LD16(lane_addr + cb * 16, acc);
+            if (chunked && u > 0) TMEM_LD16(lane_addr + 256 + cb * 16, run);
+            tmem_wait_ld();
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const int ib = b0 + cb * 16 + j;
-                if (ib < g.m) o[ib] = __uint_as_float(run[j]);
-              }
+            for (int j = 0; j < 16; ++j) {
+              const int ib = b0 + cb * 16 + j;
+              float v = 0.f;
+              if (ia < g.n && ib < g.m)
+                v = epi_value(g.epi, (int)acc[j], bh * g.n + ia, bh * g.m + ib, bh, u, g.n, g.m);
+              if (chunked) v = fadd(u > 0 ? __uint_as_float(run[j]) : 0.f, v);
+              fin[16 * h + j] = __float_as_uint(v);
             }
-          } else {
-            TMEM_ST16(lane_addr + 256 + cb * 16, run);
+            if (chunked && !last) {
+              uint32_t(&fh)[16] = *reinterpret_cast<uint32_t(*)[16]>(fin + 16 * h);
+              TMEM_ST16(lane_addr + 256 + cb * 16, fh);
+            }
           }
+          if (!chunked || last) store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, fin, lane);
         }
         if (chunked && !last) tmem_wait_st();
         tc_fence_before();

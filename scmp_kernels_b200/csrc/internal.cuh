@@ -100,6 +100,12 @@ __device__ __forceinline__ uint32_t unslice(uint32_t w) {
 //   pattern/bmap: comparator streams of b, bit t of row (bmap[j], v);
 //   the d range is split into accumulation units of unit_d dimensions (the
 //   chunks of the chunked path; one unit of d otherwise).
+constexpr int kMaxOuts = SCMP_MAX_OUT_PEERS;  // destinations of one result
+
+// Writes v to element (h, i, j) of every destination of the result.
+struct GemmArgs;
+__device__ __forceinline__ void store_out(const GemmArgs& g, int h, int i, int j, float v);
+
 struct GemmArgs {
   int batch, n, m, d;
   int L, lp, vcap;
@@ -109,11 +115,23 @@ struct GemmArgs {
   const uint32_t* pattern;
   const int32_t* bmap;
   int unit_d;
-  float* out;
   Epilogue epi;
+  // Result destinations: element (h, i, j) goes to outs[k][out_off + (h*n + i)*out_ld + j]
+  // for every k < nouts (the local output, or every device's all-gather buffer).
+  float* outs[kMaxOuts];
+  int nouts;
+  long long out_off;
+  int out_ld;
+  int out_vec;  // every destination row is 16-byte aligned (whole 4-float stores)
   int* split_acc;  // tcgen05 GEMM, split last wave: per-part integer accumulators
   int* split_cnt;  //   and per-tile arrival counters (see gemm_tc_split_bytes)
 };
+
+__device__ __forceinline__ void store_out(const GemmArgs& g, int h, int i, int j, float v) {
+  const long long idx = g.out_off + ((long long)h * g.n + i) * g.out_ld + j;
+#pragma unroll 1
+  for (int k = 0; k < g.nouts; ++k) g.outs[k][idx] = v;
+}
 
 // Host launchers (return cudaError_t of the launch).
 cudaError_t launch_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, int n_rb, int L,

@@ -272,7 +272,11 @@ int scmp_enable_matmul(const int16_t* ktab, const uint32_t* pattern, const int32
   g.pattern = pattern;
   g.bmap = bm;
   g.unit_d = d;
-  g.out = out;
+  g.outs[0] = out;
+  g.nouts = 1;
+  g.out_off = 0;
+  g.out_ld = m;
+  g.out_vec = m % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
   g.epi.kind = EPI_RAW;
   g.epi.inner = q_max_sq / (float)L;
   if (e == cudaSuccess) e = scmp::launch_gemm(g, flags, st);

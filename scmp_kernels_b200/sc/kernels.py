@@ -19,10 +19,12 @@ tables are a few KB.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import json
 import math
 import os
+import threading
 from dataclasses import dataclass
 from typing import Optional
 
@@ -239,6 +241,25 @@ def _det_kernel_tuning_active() -> bool:
 _FORCE_SIMT = os.environ.get("SCMP_FORCE_SIMT", "0") == "1"
 
 
+_REDIRECT = threading.local()
+
+
+@contextlib.contextmanager
+def output_to(peers, offset: int, ld: int, result: torch.Tensor):
+    """Within the block, every sc_matmul launch of this thread stores its
+    (batch, n, m) result at element ``offset + (h*n + i)*ld + j`` of each device
+    pointer in ``peers`` (the multi-GPU all-gather fused into the GEMM's
+    epilogue) and returns ``result`` instead of a new tensor."""
+    if not 1 <= len(peers) <= _lib.MAX_OUT_PEERS:
+        raise ValueError(f"output_to: 1..{_lib.MAX_OUT_PEERS} destinations, got {len(peers)}")
+    prev = getattr(_REDIRECT, "value", None)
+    _REDIRECT.value = ((ctypes.c_void_p * len(peers))(*peers), len(peers), int(offset), int(ld), result)
+    try:
+        yield
+    finally:
+        _REDIRECT.value = prev
+
+
 def _to_device(x: torch.Tensor) -> torch.Tensor:
     if x.device.type != "cuda":
         _lib.require_cuda()
@@ -257,7 +278,10 @@ def _launch(gran: int, mode: str, a: torch.Tensor, b: torch.Tensor, sc_prec: int
     n, d = a.shape[-2], a.shape[-1]
     m = b.shape[-2]
     dev = a.device
-    if out is None:
+    redirect = getattr(_REDIRECT, "value", None)
+    if redirect is not None:
+        peers, n_peers, out_offset, out_ld, out = redirect
+    elif out is None:
         out = torch.empty((batch, n, m) if three_d else (n, m), dtype=torch.float32, device=dev)
     amap, bmap = tables.maps_for(d, period)
     desc = _lib.MatmulDesc(
@@ -269,6 +293,10 @@ def _launch(gran: int, mode: str, a: torch.Tensor, b: torch.Tensor, sc_prec: int
         amap=amap.data_ptr(), bmap=bmap.data_ptr(), vcap=tables.vcap, lp=tables.lp,
         flags=flags | (_lib.FLAG_FORCE_SIMT if _FORCE_SIMT else 0),
         tensor_ranges=ranges.data_ptr() if ranges is not None else None)
+    if redirect is not None:
+        desc.out = None
+        desc.out_peers = ctypes.cast(peers, ctypes.c_void_p)
+        desc.n_out_peers, desc.out_offset, desc.out_ld = n_peers, out_offset, out_ld
     L = _lib.lib()
     ws_bytes = ctypes.c_size_t(0)
     _lib.check(L.scmp_sc_matmul_workspace_size(ctypes.byref(desc), ctypes.byref(ws_bytes)), "sc_matmul")

@@ -23,7 +23,7 @@ def declared_functions():
 def test_library_builds_and_loads():
     from scmp_kernels_b200 import build
     build.build()
-    assert _lib.load().scmp_abi_version() == 1
+    assert _lib.load().scmp_abi_version() == _lib.ABI_VERSION == 2
 
 
 def test_every_declared_symbol_is_exported():
@@ -48,6 +48,12 @@ def test_invalid_arguments_are_rejected_without_gpu():
     d.lp = 256
     assert lib.scmp_sc_matmul_workspace_size(ctypes.byref(d), ctypes.byref(size)) == _lib.SCMP_OK
     assert size.value >= 2 * (4 * 8 + 4 * 8)
+    d.n_out_peers = _lib.MAX_OUT_PEERS + 1
+    assert lib.scmp_sc_matmul_workspace_size(ctypes.byref(d), ctypes.byref(size)) == _lib.SCMP_ERR_INVALID_ARG
+    d.n_out_peers, d.out_ld = 2, 3  # destinations narrower than m
+    assert lib.scmp_sc_matmul_workspace_size(ctypes.byref(d), ctypes.byref(size)) == _lib.SCMP_ERR_INVALID_ARG
+    assert b"out_ld" in lib.scmp_last_error()
+    d.n_out_peers, d.out_ld = 0, 0
     d.batch, d.group_a = 2, 3
     assert lib.scmp_sc_matmul_workspace_size(ctypes.byref(d), ctypes.byref(size)) == _lib.SCMP_ERR_UNSUPPORTED
     with pytest.raises(NotImplementedError):

@@ -180,6 +180,37 @@ def test_split_last_wave_matches_whole_tiles(shape, kw, single, monkeypatch, env
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("gran,shape", [("per_row", (70, 300, 500)), ("per_tensor", (33, 90, 130)),
+                                        ("per_head", (3, 40, 50, 64))])
+@pytest.mark.parametrize("simt", [False, True])
+def test_result_scattered_to_several_buffers(gran, shape, simt, monkeypatch, env_vars):
+    """The epilogue's multi-destination store (the fused all-gather's
+    mechanism, exercised here with two buffers on one device): every buffer
+    receives the result at the given offset and row stride, nothing else."""
+    env_vars({})
+    monkeypatch.setattr(K, "_FORCE_SIMT", simt)
+    g = torch.Generator(device=DEV).manual_seed(9)
+    if gran == "per_head":
+        bh, n, m, d = shape
+        a, b = torch.randn(bh, n, d, device=DEV, generator=g), torch.randn(bh, m, d, device=DEV, generator=g)
+    else:
+        n, m, d = shape
+        bh = 1
+        a, b = torch.randn(n, d, device=DEV, generator=g), torch.randn(m, d, device=DEV, generator=g)
+    ref = sc_matmul(a, b, gran, sc_prec=8)
+    ld, off = m + 37, 11
+    bufs = [torch.full((off + bh * n * ld + 5,), float("nan"), device=DEV) for _ in range(2)]
+    with K.output_to([x.data_ptr() for x in bufs], off, ld, bufs[0]):
+        sc_matmul(a, b, gran, sc_prec=8)
+    torch.cuda.synchronize()
+    for x in bufs:
+        blk = x[off:off + bh * n * ld].view(bh * n, ld)
+        assert torch.equal(blk[:, :m], ref.reshape(bh * n, m))
+        assert torch.isnan(blk[:, m:]).all() and torch.isnan(x[:off]).all()
+        assert torch.isnan(x[off + bh * n * ld:]).all()
+    assert _lib.device_error() == 0
+
+
 def test_native_kernels_do_the_work():
     """One per_row call launches the library's own kernels: two quantisers,
     the padded row map and the SC-GEMM."""
