@@ -49,7 +49,8 @@ struct Cfg {
   static constexpr int BM = 128;                          // a rows per CTA
   static constexpr int BNL = PAIR ? 128 : 256;            // b rows per CTA
   static constexpr int TILE_A = PAIR ? 256 : 128;         // a rows per tile
-  static constexpr int TILE_B = 256;                      // b rows per tile (UMMA N)
+  static constexpr int TILE_B = 256;                      // most b rows per tile (UMMA N); the
+                                                          // schedule's tile_b <= TILE_B is used
   static constexpr int NST = ATMEM ? 4 : PAIR ? 3 : 2;    // pipeline stages
   static constexpr int A_BYTES = ATMEM ? 0 : BM * KS;     // a's bytes of a smem stage
   static constexpr int B_BYTES = BNL * KS;
@@ -67,8 +68,9 @@ struct Cfg {
   static constexpr int SMEM_BYTES = NST * STAGE_BYTES + STG_BYTES + 1024 + 256;
   static constexpr int NCTA = PAIR ? 2 : 1;
   // kind::i8, D = s32, A = B = s8, K-major; N = 256, M = 128 per SM
-  static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TILE_B >> 3) << 17) |
-                                    ((uint32_t)((PAIR ? 256 : 128) >> 4) << 24);
+  // kind::i8, D = s32, A = B = s8, K-major, M = 128 per SM; N from idesc_n()
+  static constexpr uint32_t IDESC_M = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)((PAIR ? 256 : 128) >> 4) << 24);
+  __device__ static uint32_t idesc_n(int n) { return IDESC_M | ((uint32_t)(n >> 3) << 17); }
 };
 
 // Shared-memory matrix descriptor, K-major with 128-byte swizzle: rows at a
@@ -88,31 +90,33 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 template <bool PAIR>
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t acc) {
   if constexpr (PAIR) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(Cfg<true>::IDESC), "r"(acc)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
         : "memory");
   } else {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(Cfg<false>::IDESC), "r"(acc)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
         : "memory");
   }
 }
 // M=256 N=256 K=32 pair MMA with a read from tensor memory (column a_tmem of
 // lanes 0..127 in both CTAs) and b from shared memory.
-__device__ __forceinline__ void mma_i8_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t acc) {
+__device__ __forceinline__ void mma_i8_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(bdesc), "r"(Cfg<true>::IDESC), "r"(acc)
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc)
       : "memory");
 }
 // Arrive on `bar` (same offset) in every CTA of the tile once all MMAs issued
@@ -190,13 +194,13 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
 }
 
 // Result rows ia0 .. ia0+31 (lane l holds row ia0 + l in v), columns
-// ib0 .. ib0+31, to every destination of the result (the columns < m of the
-// rows < n). The warp transposes through its 4 KB staging area `stg` so that
+// ib0 .. ib0+31, to every destination of the result (the columns < m_end, the
+// end of the tile's columns, of the rows < n). The warp transposes through its 4 KB staging area `stg` so that
 // each store instruction writes four 128-byte row segments (16 bytes per
 // lane) instead of 32 scattered words: full lines for local HBM and for a
 // peer's memory over NVLink alike. Chunks are XOR-swizzled by row, so both
 // the row-wise writes and the segment-wise reads are free of bank conflicts.
-__device__ __forceinline__ void store_rows32(const GemmArgs& g, uint32_t stg, int bh, int ia0, int ib0,
+__device__ __forceinline__ void store_rows32(const GemmArgs& g, uint32_t stg, int bh, int ia0, int ib0, int m_end,
                                              const uint32_t (&v)[32], int lane) {
 #pragma unroll
   for (int k = 0; k < 8; ++k)
@@ -209,9 +213,9 @@ __device__ __forceinline__ void store_rows32(const GemmArgs& g, uint32_t stg, in
     const int r = 4 * rr + (lane >> 3);
     const uint4 x = ld_shared_v4(stg + r * 128 + ((c ^ (r & 7)) << 4));
     const int ia = ia0 + r;
-    if (ia < g.n && ib < g.m) {
+    if (ia < g.n && ib < m_end) {
       const long long idx = g.out_off + ((long long)bh * g.n + ia) * g.out_ld + ib;
-      const bool whole = g.out_vec && ib + 3 < g.m;
+      const bool whole = g.out_vec && ib + 3 < m_end;
 #pragma unroll 1
       for (int k = 0; k < g.nouts; ++k) {
         float* o = g.outs[k] + idx;
@@ -219,9 +223,9 @@ __device__ __forceinline__ void store_rows32(const GemmArgs& g, uint32_t stg, in
           *reinterpret_cast<uint4*>(o) = x;
         } else {
           o[0] = __uint_as_float(x.x);
-          if (ib + 1 < g.m) o[1] = __uint_as_float(x.y);
-          if (ib + 2 < g.m) o[2] = __uint_as_float(x.z);
-          if (ib + 3 < g.m) o[3] = __uint_as_float(x.w);
+          if (ib + 1 < m_end) o[1] = __uint_as_float(x.y);
+          if (ib + 2 < m_end) o[2] = __uint_as_float(x.z);
+          if (ib + 3 < m_end) o[3] = __uint_as_float(x.w);
         }
       }
     }
@@ -366,8 +370,10 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
     const Work wk = work_of(sc, w, g.d);
     int bh, a0, b0;
     tile_coords(sc, wk.tile, bh, a0, b0);
-    const int row = SIDE_A ? a0 + (int)rank * C::BM + r : b0 + (int)rank * C::BNL + r;
-    const bool valid = SIDE_A ? row < g.n : row < g.m;
+    // b: the tile's tile_b rows, tile_b / NCTA per CTA (rows past them are not read)
+    const int bnl = sc.tile_b / C::NCTA;
+    const int row = SIDE_A ? a0 + (int)rank * C::BM + r : b0 + (int)rank * bnl + r;
+    const bool valid = SIDE_A ? row < g.n : (r < bnl && row < g.m);
     const int grow = bh * (SIDE_A ? g.n : g.m) + (valid ? row : 0);
     const int nu = units_of(sc, wk);
     for (int u = 0; u < nu; ++u) {
@@ -566,6 +572,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
   } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer (leader CTA)
     if (lane == 0 && leader) {
+      const uint32_t idesc = C::idesc_n(sc.tile_b);
       uint32_t it = 0, uc = 0;
       for (int w = tile0; w < sc.nwork; w += tstep) {
         const Work wk = work_of(sc, w, g.d);
@@ -587,10 +594,10 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
               const uint32_t acc = (st > 0 || kk > 0) ? 1u : 0u;
               if constexpr (ATMEM)
                 mma_i8_ts(tmem, tmem + TMEM_A_COL + s * 64 + kk * 8, smem_desc(b_base + (kk >> 2) * C::B_ATOM + off),
-                          acc);
+                          idesc, acc);
               else
                 mma_i8<PAIR>(tmem, smem_desc(a_base + (kk >> 2) * C::A_ATOM + off),
-                             smem_desc(b_base + (kk >> 2) * C::B_ATOM + off), acc);
+                             smem_desc(b_base + (kk >> 2) * C::B_ATOM + off), idesc, acc);
             }
             mma_commit<PAIR>(empty_bar(s));
           }
@@ -623,6 +630,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
       int bh, a0, b0;
       tile_coords(sc, wk.tile, bh, a0, b0);
       const int ia = a0 + (int)rank * C::BM + 32 * q + lane;
+      const int m_end = min(g.m, b0 + sc.tile_b);  // end of this tile's columns
       if (wk.part >= 0) {
         // ---- one K part of a split tile
         if (!mbar_wait(accf_bar, uc & 1, abort_flag, 5)) goto done;
@@ -633,7 +641,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
         const int rowq = 32 * q + lane;
         int* mine = g.split_acc + ((size_t)(st * sc.split + wk.part) * C::NCTA + rank) * slot_ints;
 #pragma unroll 1
-        for (int cb = 0; cb < C::TILE_B / 16; ++cb) {
+        for (int cb = 0; cb < cdiv(sc.tile_b, 16); ++cb) {
           uint32_t acc[16];
           TMEM_LD16(lane_addr + cb * 16, acc);
           tmem_wait_ld();
@@ -651,7 +659,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
           // last part to finish: the other parts' accumulators are complete
           __threadfence();
 #pragma unroll 1
-          for (int cp = 0; cp < C::TILE_B / 32; ++cp) {
+          for (int cp = 0; cp < cdiv(sc.tile_b, 32); ++cp) {
             uint32_t fin[32];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -677,12 +685,12 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
               for (int j = 0; j < 16; ++j) {
                 const int ib = b0 + cb * 16 + j;
                 fin[16 * h + j] =
-                    (ia < g.n && ib < g.m)
+                    (ia < g.n && ib < m_end)
                         ? __float_as_uint(epi_value(g.epi, (int)acc[j], bh * g.n + ia, bh * g.m + ib, bh, 0, g.n, g.m))
                         : 0u;
               }
             }
-            store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, fin, lane);
+            store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, m_end, fin, lane);
           }
         }
         tc_fence_before();
@@ -696,7 +704,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
         tc_fence_after();
         const bool last = u == sc.nunits - 1;
 #pragma unroll 1
-        for (int cp = 0; cp < C::TILE_B / 32; ++cp) {
+        for (int cp = 0; cp < cdiv(sc.tile_b, 32); ++cp) {
           uint32_t fin[32];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -709,7 +717,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
             for (int j = 0; j < 16; ++j) {
               const int ib = b0 + cb * 16 + j;
               float v = 0.f;
-              if (ia < g.n && ib < g.m)
+              if (ia < g.n && ib < m_end)
                 v = epi_value(g.epi, (int)acc[j], bh * g.n + ia, bh * g.m + ib, bh, u, g.n, g.m);
               if (chunked) v = fadd(u > 0 ? __uint_as_float(run[j]) : 0.f, v);
               fin[16 * h + j] = __float_as_uint(v);
@@ -719,7 +727,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
               TMEM_ST16(lane_addr + 256 + cb * 16, fh);
             }
           }
-          if (!chunked || last) store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, fin, lane);
+          if (!chunked || last) store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, m_end, fin, lane);
         }
         if (chunked && !last) tmem_wait_st();
         tc_fence_before();
@@ -822,9 +830,11 @@ constexpr size_t kSplitBudget = 64u << 20;  // bytes of part accumulators, at mo
 static Sched make_sched(int batch, int n, int m, int d, int unit_d, bool pair, int sms) {
   Sched s{};
   s.tile_a = pair ? Cfg<true>::TILE_A : Cfg<false>::TILE_A;
-  s.tile_b = 256;
+  // columns per tile: b's rows in equal tiles of at most 256, a multiple of 16
+  // (the MMA's N), so that a small or ragged m does not pay for 256
+  s.tiles_b = cdiv(m, 256);
+  s.tile_b = cdiv(cdiv(m, s.tiles_b), 16) * 16;
   s.tiles_a = cdiv(n, s.tile_a);
-  s.tiles_b = cdiv(m, s.tile_b);
   s.tiles = batch * s.tiles_a * s.tiles_b;
   s.unit_d = unit_d > 0 ? unit_d : d;
   s.nunits = cdiv(d, s.unit_d);
