@@ -294,14 +294,24 @@ def main():
         hs = s.cpu().pin_memory() if s is not None else None
         hy = torch.empty(y.shape, dtype=torch.float32).pin_memory()
         n_e2e = max(1, min(args.steps, 5))
-        def e2e_step():
-            da = [x.to(dev, non_blocking=True) for x in ha]
-            db = hb.to(dev, non_blocking=True)
+        if world == 1 and len(calls) == 1:
+            # the public API on pinned host operands: it streams b to the
+            # device and the result back in blocks while it computes
+            ci_host = dict(calls[0][1])
             if hs is not None:
-                for _, ci in calls:
-                    ci["smooth_scales"] = hs.to(dev, non_blocking=True)
-            yy = step(da, db)
-            hy.copy_(yy, non_blocking=True)
+                ci_host["smooth_scales"] = hs
+
+            def e2e_step():  # returns the result in pinned host memory
+                return sc_matmul(ha[0], hb, **ci_host)
+        else:
+            def e2e_step():
+                da = [x.to(dev, non_blocking=True) for x in ha]
+                db = hb.to(dev, non_blocking=True)
+                if hs is not None:
+                    for _, ci in calls:
+                        ci["smooth_scales"] = hs.to(dev, non_blocking=True)
+                yy = step(da, db)
+                hy.copy_(yy, non_blocking=True)
         e2e_step()
         torch.cuda.synchronize()
         if world > 1:

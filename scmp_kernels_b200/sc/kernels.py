@@ -189,8 +189,20 @@ def build_enable_tables(config: dict, sc_prec: int, device, stoc_len: Optional[i
     return EnableTables(ktab, pattern, amap, bmap, stoc_len, lp, G, vcap, min(ra.shape[0], rb.shape[0]))
 
 
+# The default config (config=None) of each (D, sc_prec), built once with its
+# JSON key: it is deterministic, private to this module and never mutated,
+# so a call with config=None skips serialising a D-element config.
+_DEFAULT_CONFIGS: dict = {}   # (D, sc_prec) -> config dict
+_DEFAULT_KEYS: dict = {}      # id(config dict) -> json.dumps(config, sort_keys=True)
+
+
 def _enable_table_cache_key(config: dict, sc_prec: int, device) -> str:
-    return json.dumps(config, sort_keys=True) + f"|{sc_prec}|{device}|enable"
+    base = _DEFAULT_KEYS.get(id(config))
+    if base is None or _DEFAULT_CONFIGS.get(base[1]) is not config:
+        enc = json.dumps(config, sort_keys=True)
+    else:
+        enc = base[0]
+    return enc + f"|{sc_prec}|{device}|enable"
 
 
 def _get_cached_enable_tables(config: dict, sc_prec: int, device, stoc_len: Optional[int] = None,
@@ -323,8 +335,12 @@ def _prep_smooth(a, b, smooth_scales):
 
 def _default_config(config, D, sc_prec):
     if config is None:
-        from .config_helpers import make_sobol_simple_config
-        return make_sobol_simple_config(D, D, sc_prec)
+        cfg = _DEFAULT_CONFIGS.get((D, sc_prec))
+        if cfg is None:
+            from .config_helpers import make_sobol_simple_config
+            cfg = _DEFAULT_CONFIGS[(D, sc_prec)] = make_sobol_simple_config(D, D, sc_prec)
+            _DEFAULT_KEYS[id(cfg)] = (json.dumps(cfg, sort_keys=True), (D, sc_prec))
+        return cfg
     return config
 
 

@@ -131,10 +131,85 @@ def _sc_matmul_impl(
     if granularity == "per_tensor":
         return _sc_matmul_per_tensor(a, b, mode=mode, **kw)
     if granularity == "per_row":
-        if chunk_d > 0:
-            return _sc_matmul_per_row_mlp(a, b, mode=mode, group_a=group_a, group_b=group_b,
-                                          chunk_d=chunk_d, **kw)
-        if a.dim() == 3:
-            return _sc_matmul_per_row_batched(a, b, group_a=group_a, group_b=group_b, mode=mode, **kw)
-        return _sc_matmul_per_row(a, b, group_a=group_a, group_b=group_b, mode=mode, **kw)
+        if a.dim() == 2:
+            def per_row_2d(x, y):
+                if chunk_d > 0:
+                    return _sc_matmul_per_row_mlp(x, y, mode=mode, group_a=group_a, group_b=group_b,
+                                                  chunk_d=chunk_d, **kw)
+                return _sc_matmul_per_row(x, y, group_a=group_a, group_b=group_b, mode=mode, **kw)
+            if _host_pipelined_applies(a, b):
+                return _per_row_host_pipelined(a, b, per_row_2d, group_a, group_b)
+            return per_row_2d(a, b)
+        return _sc_matmul_per_row_batched(a, b, group_a=group_a, group_b=group_b, mode=mode, **kw)
     return _sc_matmul_per_head_bipolar(a, b, **kw)
+
+
+# Host operands: the rows of a are processed in KA blocks. The first block runs
+# against b's row blocks as they arrive (b is copied to the device block by
+# block on a copy stream while the previous block computes); the later blocks
+# run against the whole of b. Each finished block of result rows (contiguous
+# in memory) is copied back on a second copy stream while the next block
+# computes. Applies to 2D per_row calls with both operands in pinned host
+# memory and a CUDA device present; per_row quantisation is row-local (row
+# groups are kept whole), so the blocks give the same bits as one call.
+_HOST_A_BLOCKS = 4        # blocks of a's rows
+_HOST_B_BLOCKS = 4        # blocks of b's rows in the first pass
+_HOST_MIN_ROWS = 1024     # smaller calls are not split
+
+
+def _host_pipelined_applies(a: torch.Tensor, b: torch.Tensor) -> bool:
+    return (a.device.type == "cpu" and b.device.type == "cpu" and torch.cuda.is_available()
+            and a.is_pinned() and b.is_pinned() and a.shape[0] >= _HOST_MIN_ROWS
+            and b.shape[0] >= _HOST_MIN_ROWS)
+
+
+def _blocks(total: int, step: int, unit: int):
+    step = max(1, (step + unit - 1) // unit) * unit  # whole row groups
+    return [(r, min(total, r + step)) for r in range(0, total, step)]
+
+
+def _per_row_host_pipelined(a: torch.Tensor, b: torch.Tensor, run, group_a: int, group_b: int) -> torch.Tensor:
+    from . import kernels as K
+    dev = torch.device("cuda", torch.cuda.current_device())
+    n, m = a.shape[0], b.shape[0]
+    a_blocks = _blocks(n, (n + _HOST_A_BLOCKS - 1) // _HOST_A_BLOCKS, group_a)
+    b_blocks = _blocks(m, (m + _HOST_B_BLOCKS - 1) // _HOST_B_BLOCKS, group_b)
+    comp = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    a_f = a if a.dtype == torch.float32 else a.float()
+    b_f = b if b.dtype == torch.float32 else b.float()
+    a_dev = torch.empty(a_f.shape, dtype=torch.float32, device=dev)
+    b_dev = torch.empty(b_f.shape, dtype=torch.float32, device=dev)
+    out_dev = torch.empty((n, m), dtype=torch.float32, device=dev)
+    out_host = torch.empty((n, m), dtype=torch.float32, pin_memory=True)
+    for t, st in ((a_dev, comp), (b_dev, comp), (out_dev, s_out)):
+        t.record_stream(st)
+    # copies in the order they are needed: a's first block, b's blocks, a's other blocks
+    ev_b = []
+    with torch.cuda.stream(s_in):
+        r0, r1 = a_blocks[0]
+        a_dev[r0:r1].copy_(a_f[r0:r1], non_blocking=True)
+        for c0, c1 in b_blocks:
+            b_dev[c0:c1].copy_(b_f[c0:c1], non_blocking=True)
+            ev_b.append(torch.cuda.Event())
+            ev_b[-1].record(s_in)
+        ev_a = [None]
+        for r0, r1 in a_blocks[1:]:
+            a_dev[r0:r1].copy_(a_f[r0:r1], non_blocking=True)
+            ev_a.append(torch.cuda.Event())
+            ev_a[-1].record(s_in)
+    for i, (r0, r1) in enumerate(a_blocks):
+        if i == 0:
+            for (c0, c1), ev in zip(b_blocks, ev_b):
+                comp.wait_event(ev)
+                with K.output_to([out_dev.data_ptr()], c0, m, out_dev):
+                    run(a_dev[r0:r1], b_dev[c0:c1])
+        else:
+            comp.wait_event(ev_a[i])
+            with K.output_to([out_dev.data_ptr()], r0 * m, m, out_dev):
+                run(a_dev[r0:r1], b_dev)
+        s_out.wait_stream(comp)
+        with torch.cuda.stream(s_out):
+            out_host[r0:r1].copy_(out_dev[r0:r1], non_blocking=True)
+    s_out.synchronize()
+    return out_host

@@ -211,6 +211,25 @@ def test_result_scattered_to_several_buffers(gran, shape, simt, monkeypatch, env
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("kw", [dict(sc_prec=8), dict(sc_prec=6, mode="unipolar", stoc_len=64, group_b=7),
+                                dict(sc_prec=8, chunk_d=64, stoc_len=128, rng_levels=128)])
+def test_host_operands_pipelined_equal_device_result(kw, env_vars):
+    """Pinned host operands take the streamed path (b and the result moved in
+    blocks while blocks compute); the result equals the device call's."""
+    env_vars({})
+    from scmp_kernels_b200.sc import matmul as MM
+    g = torch.Generator().manual_seed(4)
+    m = MM._HOST_MIN_ROWS + 333
+    a = torch.randn(MM._HOST_MIN_ROWS + 77, 256, generator=g).pin_memory()
+    b = (torch.randn(m, 256, generator=g) * 0.05).pin_memory()
+    assert MM._host_pipelined_applies(a, b)
+    y_host = sc_matmul(a, b, "per_row", **kw)
+    assert y_host.device.type == "cpu" and y_host.shape == (a.shape[0], m)
+    y_dev = sc_matmul(a.to(DEV), b.to(DEV), "per_row", **kw)
+    assert torch.equal(y_host, y_dev.cpu())
+    assert _lib.device_error() == 0
+
+
 def test_native_kernels_do_the_work():
     """One per_row call launches the library's own kernels: two quantisers,
     the padded row map and the SC-GEMM."""
