@@ -242,6 +242,38 @@ def test_native_kernels_do_the_work():
     assert _lib.launch_count() - n0 == 4
 
 
+@pytest.mark.parametrize("workload,rows", [("config2", None), ("config5", 512), ("config3qk", None),
+                                            ("config3av", None)])
+def test_full_size_workloads_agree_across_gemm_variants(workload, rows, monkeypatch, env_vars):
+    """The benchmark workloads at their full sizes (config 5: its first 512
+    rows of a against all of b; per_row quantisation is row-local, so a row
+    slice is an exact sub-problem): the default GEMM (SM pairs, a in tensor
+    memory, split last wave), SM pairs with a in shared memory, and the
+    CUDA-core GEMM give the same bits, and every output is finite."""
+    env_vars({})
+    from scmp_kernels_b200 import workloads as W
+    if workload == "config2":
+        a, b = W.config2(DEV)
+        kw = dict(granularity="per_row", mode="bipolar", sc_prec=8)
+    elif workload == "config5":
+        a, b, s5 = W.config5(DEV)
+        a = a[:rows].contiguous()
+        kw = dict(granularity="per_row", mode="unipolar", sc_prec=6, stoc_len=64, smooth_scales=s5)
+    else:
+        q, k, probs, v_t = W.config3(DEV)
+        a, b = (q, k) if workload == "config3qk" else (probs, v_t)
+        kw = dict(granularity="per_head", sc_prec=8)
+    outs = []
+    for simt, asmem in ((False, "0"), (False, "1"), (True, "0")):
+        monkeypatch.setattr(K, "_FORCE_SIMT", simt)
+        monkeypatch.setenv("SCMP_TC_ASMEM", asmem)
+        outs.append(sc_matmul(a, b, **kw))
+    assert torch.isfinite(outs[0]).all()
+    for i, o in enumerate(outs[1:], 1):
+        assert torch.equal(outs[0], o), f"variant {i} differs"
+    assert _lib.device_error() == 0
+
+
 def test_quantiser_api_vs_oracle():
     from scmp_kernels_b200 import quant as Q
     g = torch.Generator().manual_seed(3)
