@@ -150,6 +150,7 @@ static void carve(const scmp_matmul_desc* d, Carver& c, Plan& p) {
 static QuantArgs base_quant(const scmp_matmul_desc* d, bool side_a, int q) {
   QuantArgs a{};
   a.x = side_a ? d->a : d->b;
+  a.vec = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && d->d % 4 == 0;
   a.rows_per_batch = side_a ? d->n : d->m;
   a.rows = d->batch * a.rows_per_batch;
   a.d = d->d;

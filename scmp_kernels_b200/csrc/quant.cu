@@ -27,20 +27,50 @@ __device__ __forceinline__ int16_t encode(const QuantArgs& q, int j, int boundar
 // statistics
 // --------------------------------------------------------------------------
 
-// stats[r] = {absmax, max, min} of (smoothed) row r; one warp per row.
-__global__ void row_stats_kernel(QuantArgs q, float* __restrict__ stats) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= q.rows) return;
-  float am = 0.f, mx = -INFINITY, mn = INFINITY;
-  for (int j = lane; j < q.d; j += 32) {
-    const float x = load_x(q, warp, j);
-    am = fmaxf(am, fabsf(x));
-    mx = fmaxf(mx, x);
-    mn = fminf(mn, x);
+// {absmax, max, min} of (smoothed) row `row`, reduced over the warp. With
+// q.vec the row is read as float4, four loads in flight per lane.
+__device__ __forceinline__ void row_minmax(const QuantArgs& q, int row, int lane, float& am, float& mx, float& mn) {
+  am = 0.f;
+  mx = -INFINITY;
+  mn = INFINITY;
+  if (q.vec) {
+    const float4* src = reinterpret_cast<const float4*>(q.x + (size_t)row * q.d);
+    const int n4 = q.d >> 2;
+#pragma unroll 4
+    for (int k = lane; k < n4; k += 32) {
+      const float4 v = __ldg(src + k);
+      float xs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float x = xs[e];
+        if (q.smooth) {
+          const float sv = __ldg(q.smooth + 4 * k + e);
+          x = q.smooth_div ? fdiv(x, sv) : fmul(x, sv);
+        }
+        am = fmaxf(am, fabsf(x));
+        mx = fmaxf(mx, x);
+        mn = fminf(mn, x);
+      }
+    }
+  } else {
+    for (int j = lane; j < q.d; j += 32) {
+      const float x = load_x(q, row, j);
+      am = fmaxf(am, fabsf(x));
+      mx = fmaxf(mx, x);
+      mn = fminf(mn, x);
+    }
   }
   am = warp_max(am);
   mx = warp_max(mx);
   mn = warp_min(mn);
+}
+
+// stats[r] = {absmax, max, min} of (smoothed) row r; one warp per row.
+__global__ void row_stats_kernel(QuantArgs q, float* __restrict__ stats) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= q.rows) return;
+  float am, mx, mn;
+  row_minmax(q, warp, lane, am, mx, mn);
   if (lane == 0) {
     stats[3 * (size_t)warp + 0] = am;
     stats[3 * (size_t)warp + 1] = mx;
@@ -198,6 +228,43 @@ __global__ void tensor_params_kernel(const float* __restrict__ stats_a, int rows
 // quantisers: one warp per row
 // --------------------------------------------------------------------------
 
+// One element of the non-chunked recipes: the quantised value's boundary
+// (through the k-table for operand a) with its sign, as the GEMM operand.
+template <int R>
+__device__ __forceinline__ int16_t quant_one(const QuantArgs& q, int j, float x, float sc, float inv, float zp,
+                                            float qf, float& rsum) {
+  {
+    int bnd;
+    float sgn = 1.f;
+    if (R == Q_TENSOR_BIP || R == Q_HEAD_BIP) {
+      // fused.py:94-106 / 265-273: clamp(rint(x * inv), [qmin, q]); rint(|xc| * G/q)
+      const float xc = fclamp(frint(fmul(x, inv)), q.qmin, qf);
+      bnd = (int)frint(fmul(fabsf(xc), q.ratio));
+      sgn = xc;
+    } else if (R == Q_TENSOR_UNI) {
+      // fused.py:84, 98, 114-121: clamp(rint(x * inv + zp), 0, q)
+      const float xc = fclamp(frint(fadd(fmul(x, inv), zp)), 0.f, qf);
+      bnd = (int)frint(fmul(xc, q.ratio));
+      rsum = fadd(rsum, xc);
+    } else if (R == Q_GROUP_SYM) {
+      // grouped.py:51 + kernels.py:1679: clamp(round(x / s), +-q); round(|xi| * G / q)
+      const float xi = fclamp(frint(fdiv(x, sc)), -qf, qf);
+      bnd = (int)frint(fdiv(fmul(fabsf(xi), (float)q.G), qf));
+      sgn = xi;
+    } else if (R == Q_BATCH_SYM) {
+      // grouped.py:148/156 + kernels.py:1864: round(|xi| * fl32(G / q))
+      const float xi = fclamp(frint(fdiv(x, sc)), -qf, qf);
+      bnd = (int)frint(fmul(fabsf(xi), q.ratio));
+      sgn = xi;
+    } else {  // Q_GROUP_ASYM: grouped.py:131 + kernels.py:1685
+      const float xi = fclamp(frint(fadd(fdiv(x, sc), zp)), 0.f, qf);
+      bnd = (int)frint(fdiv(fmul(xi, (float)q.G), qf));
+      rsum = fadd(rsum, xi);
+    }
+    return encode(q, j, bnd, sgn);
+  }
+}
+
 template <int R>
 __global__ void quant_rows_kernel(QuantArgs q) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -233,16 +300,8 @@ __global__ void quant_rows_kernel(QuantArgs q) {
     inv = __ldg(q.params + row / q.rows_per_batch);
   } else if (q.self_stats) {
     // G == 1: the row is its own group (grouped.py:46-47, 111-115)
-    float am = 0.f, mx = -INFINITY, mn = INFINITY;
-    for (int j = lane; j < q.d; j += 32) {
-      const float x = load_x(q, row, j);
-      am = fmaxf(am, fabsf(x));
-      mx = fmaxf(mx, x);
-      mn = fminf(mn, x);
-    }
-    am = warp_max(am);
-    mx = warp_max(mx);
-    mn = warp_min(mn);
+    float am, mx, mn;
+    row_minmax(q, row, lane, am, mx, mn);
     if (R == Q_GROUP_ASYM) {
       sc = fdiv(fmaxf(fsub(mx, mn), 1e-5f), qf);
       zp = fclamp(frint(fdiv(-mn, sc)), 0.f, qf);
@@ -259,36 +318,42 @@ __global__ void quant_rows_kernel(QuantArgs q) {
   }
 
   float rsum = 0.f;
-  for (int j = lane; j < q.d; j += 32) {
-    const float x = load_x(q, row, j);
-    int bnd;
-    float sgn = 1.f;
-    if (R == Q_TENSOR_BIP || R == Q_HEAD_BIP) {
-      // fused.py:94-106 / 265-273: clamp(rint(x * inv), [qmin, q]); rint(|xc| * G/q)
-      const float xc = fclamp(frint(fmul(x, inv)), q.qmin, qf);
-      bnd = (int)frint(fmul(fabsf(xc), q.ratio));
-      sgn = xc;
-    } else if (R == Q_TENSOR_UNI) {
-      // fused.py:84, 98, 114-121: clamp(rint(x * inv + zp), 0, q)
-      const float xc = fclamp(frint(fadd(fmul(x, inv), zp)), 0.f, qf);
-      bnd = (int)frint(fmul(xc, q.ratio));
-      rsum = fadd(rsum, xc);
-    } else if (R == Q_GROUP_SYM) {
-      // grouped.py:51 + kernels.py:1679: clamp(round(x / s), +-q); round(|xi| * G / q)
-      const float xi = fclamp(frint(fdiv(x, sc)), -qf, qf);
-      bnd = (int)frint(fdiv(fmul(fabsf(xi), (float)q.G), qf));
-      sgn = xi;
-    } else if (R == Q_BATCH_SYM) {
-      // grouped.py:148/156 + kernels.py:1864: round(|xi| * fl32(G / q))
-      const float xi = fclamp(frint(fdiv(x, sc)), -qf, qf);
-      bnd = (int)frint(fmul(fabsf(xi), q.ratio));
-      sgn = xi;
-    } else {  // Q_GROUP_ASYM: grouped.py:131 + kernels.py:1685
-      const float xi = fclamp(frint(fadd(fdiv(x, sc), zp)), 0.f, qf);
-      bnd = (int)frint(fdiv(fmul(xi, (float)q.G), qf));
-      rsum = fadd(rsum, xi);
+  // Each lane quantises whole blocks of eight dimensions (blocked output: one
+  // 16-byte store per block; with q.vec, two 16-byte loads per block).
+  const int nb = d8(q.d);
+#pragma unroll 2
+  for (int jb = lane; jb < nb; jb += 32) {
+    const int j0 = 8 * jb;
+    float xs[8];
+    if (q.vec && j0 + 8 <= q.d) {
+      const float4* src = reinterpret_cast<const float4*>(q.x + (size_t)row * q.d + j0);
+      const float4 u = __ldg(src), w = __ldg(src + 1);
+      xs[0] = u.x; xs[1] = u.y; xs[2] = u.z; xs[3] = u.w;
+      xs[4] = w.x; xs[5] = w.y; xs[6] = w.z; xs[7] = w.w;
+      if (q.smooth) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float sv = __ldg(q.smooth + j0 + e);
+          xs[e] = q.smooth_div ? fdiv(xs[e], sv) : fmul(xs[e], sv);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xs[e] = j0 + e < q.d ? load_x(q, row, j0 + e) : 0.f;
     }
-    out[blk_idx(q.rows, row, j)] = encode(q, j, bnd, sgn);
+    uint32_t packed[4];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int j = j0 + e;
+      const float x = xs[e];
+      int16_t code = 0;
+      if (j < q.d) code = quant_one<R>(q, j, x, sc, inv, zp, qf, rsum);
+      if (e & 1)
+        packed[e >> 1] |= (uint32_t)(uint16_t)code << 16;
+      else
+        packed[e >> 1] = (uint16_t)code;
+    }
+    *reinterpret_cast<uint4*>(out + blk_idx(q.rows, row, j0)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
   }
   if (q.row_sum) {
     rsum = warp_sum(rsum);

@@ -20,6 +20,7 @@ enum GroupRecipe { GP_SYM = 0, GP_ASYM = 1, GP_HEAD = 2 };
 struct QuantArgs {
   const float* x;  // (rows, d) float32, rows = batch * rows_per_batch
   int rows, d, rows_per_batch;
+  int vec;         // x is 16-byte aligned and d % 4 == 0 (rows read as float4)
   const float* smooth;  // (d,) or NULL
   int smooth_div;       // 1: x / s (operand a), 0: x * s (operand b)
   int q;                // q_max
