@@ -65,7 +65,8 @@ struct Cfg {
   static constexpr int THREADS = NWARPS * 32;
   // epilogue staging: 4 warps x 32 rows x 32 result columns (float32)
   static constexpr int STG_BYTES = 4 * 32 * 32 * 4;
-  static constexpr int SMEM_BYTES = NST * STAGE_BYTES + STG_BYTES + 1024 + 256;
+  static constexpr int SB_BYTES = TILE_B * 4;            // a chunk's column scales (chunked path)
+  static constexpr int SMEM_BYTES = NST * STAGE_BYTES + STG_BYTES + SB_BYTES + 1024 + 256;
   static constexpr int NCTA = PAIR ? 2 : 1;
   // kind::i8, D = s32, A = B = s8, K-major; N = 256, M = 128 per SM
   // kind::i8, D = s32, A = B = s8, K-major, M = 128 per SM; N from idesc_n()
@@ -176,6 +177,16 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
       "r"((r)[0]), "r"((r)[1]), "r"((r)[2]), "r"((r)[3]), "r"((r)[4]), "r"((r)[5]), "r"((r)[6]),  \
       "r"((r)[7]), "r"((r)[8]), "r"((r)[9]), "r"((r)[10]), "r"((r)[11]), "r"((r)[12]),             \
       "r"((r)[13]), "r"((r)[14]), "r"((r)[15]))
+
+#define TMEM_LD8(taddr, r)                                                                         \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"            \
+               : "=r"((r)[0]), "=r"((r)[1]), "=r"((r)[2]), "=r"((r)[3]), "=r"((r)[4]), "=r"((r)[5]), \
+                 "=r"((r)[6]), "=r"((r)[7])                                                         \
+               : "r"(taddr))
+#define TMEM_ST8(taddr, r)                                                                         \
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), \
+               "r"((r)[0]), "r"((r)[1]), "r"((r)[2]), "r"((r)[3]), "r"((r)[4]), "r"((r)[5]), "r"((r)[6]), \
+               "r"((r)[7]))
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -515,15 +526,16 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
   const uint32_t sbase = (raw + 1023u) & ~1023u;  // SW128 tiles need 1024-B alignment; the
   uint8_t* gbase = smem_raw + (sbase - raw);      // offset is the same in both CTAs of a pair
   const uint32_t stg_base = sbase + NST * C::STAGE_BYTES;   // epilogue staging
-  const uint32_t bar_base = stg_base + C::STG_BYTES;
+  float* sbs = reinterpret_cast<float*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES);  // chunk column scales
+  const uint32_t bar_base = stg_base + C::STG_BYTES + C::SB_BYTES;
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (NST + s); };
   const uint32_t accf_bar = bar_base + 8u * (2 * NST);
   const uint32_t acce_bar = bar_base + 8u * (2 * NST + 1);
   const uint32_t drain_bar = bar_base + 8u * (2 * NST + 2);
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + 128);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + 136);
-  volatile int* split_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + 144);
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + C::SB_BYTES + 128);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + C::SB_BYTES + 136);
+  volatile int* split_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + C::SB_BYTES + 144);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_rank() : 0u;   // CTA rank inside the pair
@@ -703,6 +715,57 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
         if (!mbar_wait(accf_bar, uc & 1, abort_flag, 5)) goto done;
         tc_fence_after();
         const bool last = u == sc.nunits - 1;
+        if (chunked && !last) {
+          // Chunk u of several: add its scaled values to the running sum in
+          // tensor-memory columns 256+. The chunk's column scales are staged
+          // in shared memory, and slice cb+1 is loaded while cb is processed.
+          const int et = (warp - C::EPI_WARP0) * 32 + lane;
+          asm volatile("bar.sync 1, 128;" ::: "memory");  // the previous chunk's readers are done
+          for (int c = et; c < sc.tile_b; c += 128)
+            sbs[c] = b0 + c < g.m ? __ldg(g.epi.sb + (size_t)u * g.m + b0 + c) : 0.f;
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          const float sar = ia < g.n ? __ldg(g.epi.sa + (size_t)u * g.n + ia) : 0.f;
+          const int ns = cdiv(sc.tile_b, 8);  // slices of eight columns
+          uint32_t acc0[8], run0[8], acc1[8], run1[8];
+          // result of slice cb into acc (in place), stored to the running sum
+          auto chunk_slice = [&](int cb, uint32_t (&acc)[8], const uint32_t (&run)[8]) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int ib = b0 + cb * 8 + j;
+              float x = 0.f;
+              if (ia < g.n && ib < m_end)
+                x = fmul(fmul((float)(int)acc[j], g.epi.inner), fmul(sar, sbs[cb * 8 + j]));
+              acc[j] = __float_as_uint(fadd(u > 0 ? __uint_as_float(run[j]) : 0.f, x));
+            }
+            TMEM_ST8(lane_addr + 256 + cb * 8, acc);
+          };
+          TMEM_LD8(lane_addr, acc0);
+          if (u > 0) TMEM_LD8(lane_addr + 256, run0);
+#pragma unroll 1
+          for (int cb = 0; cb < ns; cb += 2) {
+            tmem_wait_ld();
+            if (cb + 1 < ns) {
+              TMEM_LD8(lane_addr + (cb + 1) * 8, acc1);
+              if (u > 0) TMEM_LD8(lane_addr + 256 + (cb + 1) * 8, run1);
+            }
+            chunk_slice(cb, acc0, run0);
+            if (cb + 1 < ns) {
+              tmem_wait_ld();
+              tmem_wait_st();  // acc0 is about to be reloaded; its store has read it
+              if (cb + 2 < ns) {
+                TMEM_LD8(lane_addr + (cb + 2) * 8, acc0);
+                if (u > 0) TMEM_LD8(lane_addr + 256 + (cb + 2) * 8, run0);
+              }
+              chunk_slice(cb + 1, acc1, run1);
+              tmem_wait_st();  // likewise acc1
+            }
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar, rank);
+          continue;
+        }
 #pragma unroll 1
         for (int cp = 0; cp < cdiv(sc.tile_b, 32); ++cp) {
           uint32_t fin[32];
@@ -722,14 +785,9 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
               if (chunked) v = fadd(u > 0 ? __uint_as_float(run[j]) : 0.f, v);
               fin[16 * h + j] = __float_as_uint(v);
             }
-            if (chunked && !last) {
-              uint32_t(&fh)[16] = *reinterpret_cast<uint32_t(*)[16]>(fin + 16 * h);
-              TMEM_ST16(lane_addr + 256 + cb * 16, fh);
-            }
           }
-          if (!chunked || last) store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, m_end, fin, lane);
+          store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, m_end, fin, lane);
         }
-        if (chunked && !last) tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar, rank);
