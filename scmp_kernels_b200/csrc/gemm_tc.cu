@@ -530,9 +530,13 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
   const uint32_t bar_base = stg_base + C::STG_BYTES + C::SB_BYTES;
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (NST + s); };
-  const uint32_t accf_bar = bar_base + 8u * (2 * NST);
-  const uint32_t acce_bar = bar_base + 8u * (2 * NST + 1);
-  const uint32_t drain_bar = bar_base + 8u * (2 * NST + 2);
+  // accumulator buffers: two (tensor-memory columns [0,256) and [256,512))
+  // when those columns are free (a in shared memory, one accumulation unit per
+  // tile), so that a tile's epilogue overlaps the next tile's MMAs; else one
+  const int nbuf = (!ATMEM && sc.nunits == 1) ? 2 : 1;
+  auto accf_bar = [&](int b) { return bar_base + 8u * (2 * NST + b); };
+  auto acce_bar = [&](int b) { return bar_base + 8u * (2 * NST + 2 + b); };
+  const uint32_t drain_bar = bar_base + 8u * (2 * NST + 4);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + C::SB_BYTES + 128);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + C::SB_BYTES + 136);
   volatile int* split_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + C::SB_BYTES + 144);
@@ -549,8 +553,10 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
         mbar_init(full_bar(s), C::NCTA * C::PROD_WARPS);  // one arrival per producer warp of the tile
         mbar_init(empty_bar(s), 1);
       }
-      mbar_init(accf_bar, 1);
-      mbar_init(acce_bar, C::NCTA * 4);                  // one arrival per epilogue warp of the tile
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(accf_bar(b), 1);
+        mbar_init(acce_bar(b), C::NCTA * 4);  // one arrival per epilogue warp of the tile
+      }
       mbar_init(drain_bar, 1);
       *abort_flag = 0;
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -590,7 +596,9 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
         const Work wk = work_of(sc, w, g.d);
         const int nu = units_of(sc, wk);
         for (int u = 0; u < nu; ++u, ++uc) {
-          if (!mbar_wait(acce_bar, (uc & 1) ^ 1, abort_flag, 4)) goto mma_done;
+          const int buf = (int)(uc % nbuf);
+          if (!mbar_wait(acce_bar(buf), ((uc / nbuf) & 1) ^ 1, abort_flag, 4)) goto mma_done;
+          const uint32_t tacc = tmem + (uint32_t)buf * 256;
           tc_fence_after();
           int d0, d1;
           unit_range(sc, wk, u, g.d, d0, d1);
@@ -605,15 +613,15 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
               const uint32_t off = (kk & 3) * 32;
               const uint32_t acc = (st > 0 || kk > 0) ? 1u : 0u;
               if constexpr (ATMEM)
-                mma_i8_ts(tmem, tmem + TMEM_A_COL + s * 64 + kk * 8, smem_desc(b_base + (kk >> 2) * C::B_ATOM + off),
+                mma_i8_ts(tacc, tmem + TMEM_A_COL + s * 64 + kk * 8, smem_desc(b_base + (kk >> 2) * C::B_ATOM + off),
                           idesc, acc);
               else
-                mma_i8<PAIR>(tmem, smem_desc(a_base + (kk >> 2) * C::A_ATOM + off),
+                mma_i8<PAIR>(tacc, smem_desc(a_base + (kk >> 2) * C::A_ATOM + off),
                              smem_desc(b_base + (kk >> 2) * C::B_ATOM + off), idesc, acc);
             }
             mma_commit<PAIR>(empty_bar(s));
           }
-          mma_commit<PAIR>(accf_bar);
+          mma_commit<PAIR>(accf_bar(buf));
         }
       }
     mma_done:
@@ -645,9 +653,11 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
       const int m_end = min(g.m, b0 + sc.tile_b);  // end of this tile's columns
       if (wk.part >= 0) {
         // ---- one K part of a split tile
-        if (!mbar_wait(accf_bar, uc & 1, abort_flag, 5)) goto done;
+        const int buf = (int)(uc % nbuf);
+        if (!mbar_wait(accf_bar(buf), (uc / nbuf) & 1, abort_flag, 5)) goto done;
         ++uc;
         tc_fence_after();
+        const uint32_t acc_addr = lane_addr + (uint32_t)buf * 256;
         const int st = wk.tile - sc.full;
         const size_t slot_ints = (size_t)C::BM * C::TILE_B;
         const int rowq = 32 * q + lane;
@@ -655,7 +665,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
 #pragma unroll 1
         for (int cb = 0; cb < cdiv(sc.tile_b, 16); ++cb) {
           uint32_t acc[16];
-          TMEM_LD16(lane_addr + cb * 16, acc);
+          TMEM_LD16(acc_addr + cb * 16, acc);
           tmem_wait_ld();
           int4* dst = reinterpret_cast<int4*>(mine + ((size_t)cb * C::BM + rowq) * 16);
 #pragma unroll
@@ -677,7 +687,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
             for (int h = 0; h < 2; ++h) {
               const int cb = 2 * cp + h;
               uint32_t acc[16];
-              TMEM_LD16(lane_addr + cb * 16, acc);
+              TMEM_LD16(acc_addr + cb * 16, acc);
               tmem_wait_ld();
               for (int p = 0; p < sc.split; ++p) {
                 if (p == wk.part) continue;
@@ -707,13 +717,15 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar, rank);
+        if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar(buf), rank);
         continue;
       }
       const bool chunked = g.epi.kind == EPI_CHUNK;
       for (int u = 0; u < sc.nunits; ++u, ++uc) {
-        if (!mbar_wait(accf_bar, uc & 1, abort_flag, 5)) goto done;
+        const int buf = (int)(uc % nbuf);
+        if (!mbar_wait(accf_bar(buf), (uc / nbuf) & 1, abort_flag, 5)) goto done;
         tc_fence_after();
+        const uint32_t acc_addr = lane_addr + (uint32_t)buf * 256;  // running sum: lane_addr + 256
         const bool last = u == sc.nunits - 1;
         if (chunked && !last) {
           // Chunk u of several: add its scaled values to the running sum in
@@ -739,13 +751,13 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
             }
             TMEM_ST8(lane_addr + 256 + cb * 8, acc);
           };
-          TMEM_LD8(lane_addr, acc0);
+          TMEM_LD8(acc_addr, acc0);
           if (u > 0) TMEM_LD8(lane_addr + 256, run0);
 #pragma unroll 1
           for (int cb = 0; cb < ns; cb += 2) {
             tmem_wait_ld();
             if (cb + 1 < ns) {
-              TMEM_LD8(lane_addr + (cb + 1) * 8, acc1);
+              TMEM_LD8(acc_addr + (cb + 1) * 8, acc1);
               if (u > 0) TMEM_LD8(lane_addr + 256 + (cb + 1) * 8, run1);
             }
             chunk_slice(cb, acc0, run0);
@@ -753,7 +765,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
               tmem_wait_ld();
               tmem_wait_st();  // acc0 is about to be reloaded; its store has read it
               if (cb + 2 < ns) {
-                TMEM_LD8(lane_addr + (cb + 2) * 8, acc0);
+                TMEM_LD8(acc_addr + (cb + 2) * 8, acc0);
                 if (u > 0) TMEM_LD8(lane_addr + 256 + (cb + 2) * 8, run0);
               }
               chunk_slice(cb + 1, acc1, run1);
@@ -763,7 +775,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar, rank);
+          if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar(buf), rank);
           continue;
         }
 #pragma unroll 1
@@ -773,7 +785,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
           for (int h = 0; h < 2; ++h) {
             const int cb = 2 * cp + h;
             uint32_t acc[16], run[16];
-            TMEM_LD16(lane_addr + cb * 16, acc);
+            TMEM_LD16(acc_addr + cb * 16, acc);
             if (chunked && u > 0) TMEM_LD16(lane_addr + 256 + cb * 16, run);
             tmem_wait_ld();
 #pragma unroll
@@ -790,7 +802,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar, rank);
+        if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar(buf), rank);
       }
     }
   }
@@ -866,6 +878,10 @@ static bool use_pair() {
   const char* e = getenv("SCMP_TC_SINGLE");
   return !(e && e[0] == '1');
 }
+
+// Tiles with fewer K stages than this use two accumulators rather than a in
+// tensor memory (the epilogue is then a visible share of a tile).
+constexpr int kShortTileStages = 512;
 
 static int device_sms() {
   int dev = 0, sms = 148;
@@ -952,8 +968,12 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
   const int spd = g.lp / tlen;
   // a in tensor memory needs the running-sum columns free: one accumulation
   // unit per tile (SCMP_TC_ASMEM=1 keeps a in shared memory)
+  // short tiles (few K stages) instead keep a in shared memory, which frees
+  // the tensor-memory columns for a second accumulator: the epilogue of one
+  // tile then overlaps the next tile's MMAs
   const char* asmem = getenv("SCMP_TC_ASMEM");
-  if (pair && s.nunits == 1 && !(asmem && asmem[0] == '1')) {
+  const int stages_per_tile = (tlen < 256 ? cdiv(g.d, 256 / tlen) : g.d) * spd;
+  if (pair && s.nunits == 1 && stages_per_tile >= kShortTileStages && !(asmem && asmem[0] == '1')) {
     switch (tlen) {
       case 32: return launch_t<32, 1, true, true>(g, s, sms, st);
       case 64: return launch_t<64, 1, true, true>(g, s, sms, st);
