@@ -97,6 +97,19 @@ def clocks_start(idx):
     return p, f.name
 
 
+def clocks_wait_first_sample(path, timeout_s=10.0):
+    """Block until the sampler has written its first line, so that its start-up
+    (NVML initialisation) happens before the timed region, not inside it."""
+    t0 = time.time()
+    while time.time() - t0 < timeout_s:
+        try:
+            if os.path.getsize(path) > 0:
+                return
+        except OSError:
+            pass
+        time.sleep(0.05)
+
+
 def clocks_stop(p, path):
     if p is None:
         return None
@@ -239,6 +252,8 @@ def main():
         return y
 
     clk_p, clk_f = clocks_start(local)  # sampled from warm-up to the end of the timed steps
+    if clk_p is not None:
+        clocks_wait_first_sample(clk_f)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
