@@ -136,12 +136,13 @@ static void carve(const scmp_matmul_desc* d, Carver& c, Plan& p) {
   p.scal = c.take<float>(8);
   if (!(d->flags & (SCMP_FLAG_FORCE_SIMT | SCMP_FLAG_NO_SPLIT))) {
     const int unit_d = p.chunked ? d->chunk_d : d->d;
-    const size_t bytes = gemm_tc_split_bytes(d->batch, d->n, d->m, d->d, unit_d);
+    const size_t bytes = gemm_tc_split_bytes(d->batch, d->n, d->m, d->d, unit_d, d->lp);
     if (bytes) {
       char* blk = c.take<char>(bytes);
       if (blk) {
         p.split_acc = reinterpret_cast<int*>(blk);
-        p.split_cnt = reinterpret_cast<int*>(blk + gemm_tc_split_cnt_offset(d->batch, d->n, d->m, d->d, unit_d));
+        p.split_cnt =
+            reinterpret_cast<int*>(blk + gemm_tc_split_cnt_offset(d->batch, d->n, d->m, d->d, unit_d, d->lp));
       }
     }
   }

@@ -35,23 +35,34 @@ namespace tc {
 
 constexpr int KS = 256;                    // K bytes per stage
 constexpr int PROD_A_WARPS = 4;            // 128 a rows per CTA
-// Tensor memory: [0,256) accumulator; [256,512) either the running chunk sum
-// (chunked path) or, with A in tensor memory, a's stages (64 columns each).
+// Tensor memory (512 columns): the accumulator from column 0; after it, the
+// running chunk sum (chunked path, [256,512)), a second accumulator (short
+// tiles, [256,512)) or, with a in tensor memory, a's stages (64 columns each).
 constexpr int TMEM_COLS = 512;
-constexpr int TMEM_A_COL = 256;
 
 // ATMEM (2-SM variant, one accumulation unit per tile): a's stages live in
 // tensor memory, written by the producers with tcgen05.st and read by the
-// MMA from there, so shared memory carries only b (half the traffic).
-template <bool PAIR, bool ATMEM = false>
+// MMA from there, so shared memory carries only b. WIDE (with ATMEM, for
+// streams shorter than 256): up to 320 b rows per tile, computed as two MMAs
+// of half the width per K step (the MMA's N is at most 256), so that each
+// expanded a stage serves 320 columns; the accumulator takes columns [0,320)
+// and a's three stages [320,512). (With 256-long streams the fifth b warp on
+// one SM sub-partition costs more than the wider tile gains.)
+template <int TLEN>
+__host__ __device__ constexpr bool wide_tiles() { return TLEN < 256; }
+
+template <bool PAIR, bool ATMEM = false, bool WIDE_ = false>
 struct Cfg {
   static_assert(PAIR || !ATMEM, "a in tensor memory is implemented for SM pairs");
+  static_assert(ATMEM || !WIDE_, "wide tiles need a in tensor memory");
+  static constexpr bool WIDE = WIDE_;                     // two half-width MMAs per K step
   static constexpr int BM = 128;                          // a rows per CTA
-  static constexpr int BNL = PAIR ? 128 : 256;            // b rows per CTA
   static constexpr int TILE_A = PAIR ? 256 : 128;         // a rows per tile
-  static constexpr int TILE_B = 256;                      // most b rows per tile (UMMA N); the
+  static constexpr int TILE_B = WIDE ? 320 : 256;         // most b rows per tile; the
                                                           // schedule's tile_b <= TILE_B is used
-  static constexpr int NST = ATMEM ? 4 : PAIR ? 3 : 2;    // pipeline stages
+  static constexpr int BNL = TILE_B / (PAIR ? 2 : 1);     // b rows per CTA
+  static constexpr int TMEM_A = TILE_B;                   // first tensor-memory column of a's stages
+  static constexpr int NST = WIDE ? 3 : ATMEM ? 4 : PAIR ? 3 : 2;  // pipeline stages
   static constexpr int A_BYTES = ATMEM ? 0 : BM * KS;     // a's bytes of a smem stage
   static constexpr int B_BYTES = BNL * KS;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -364,7 +375,7 @@ template <bool SIDE_A, int TLEN, int SPD, bool PAIR, bool ATMEM>
 __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint32_t sbase, uint32_t bar_base,
                                         volatile int* abort_flag, uint32_t rank, int tile0, int tstep, int r,
                                         int lane, uint32_t tmem_a) {
-  using C = Cfg<PAIR, ATMEM>;
+  using C = Cfg<PAIR, ATMEM, ATMEM && wide_tiles<TLEN>()>;
   constexpr int NST = C::NST;
   constexpr int DPS = TLEN < 256 ? 256 / TLEN : 1;
   constexpr int NSPB = SPB<TLEN, SPD>();
@@ -381,9 +392,18 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
     const Work wk = work_of(sc, w, g.d);
     int bh, a0, b0;
     tile_coords(sc, wk.tile, bh, a0, b0);
-    // b: the tile's tile_b rows, tile_b / NCTA per CTA (rows past them are not read)
+    // b: the tile's tile_b rows, tile_b / NCTA per CTA (rows past them are not
+    // read). A pair MMA of width N takes its first N/2 columns from CTA 0's
+    // rows and the rest from CTA 1's; wide tiles stack two such MMAs of width
+    // nh = tile_b / 2, so smem row r of CTA c is column h*nh + c*nh/2 + r' of
+    // the tile (h = r / (nh/2), r' = r % (nh/2)).
     const int bnl = sc.tile_b / C::NCTA;
-    const int row = SIDE_A ? a0 + (int)rank * C::BM + r : b0 + (int)rank * bnl + r;
+    int bcol = (int)rank * bnl + r;
+    if constexpr (C::WIDE) {
+      const int hh = sc.tile_b / 4;
+      bcol = (r / hh) * (2 * hh) + (int)rank * hh + r % hh;
+    }
+    const int row = SIDE_A ? a0 + (int)rank * C::BM + r : b0 + bcol;
     const bool valid = SIDE_A ? row < g.n : (r < bnl && row < g.m);
     const int grow = bh * (SIDE_A ? g.n : g.m) + (valid ? row : 0);
     const int nu = units_of(sc, wk);
@@ -518,8 +538,9 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
 // TLEN: padded stream length lp when lp <= 256 (256/lp dimensions per stage),
 // or 256 when lp = 256*SPD (SPD stages per dimension, SPD = 1 or 2).
 template <int TLEN, int SPD, bool PAIR, bool ATMEM>
-__global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched sc) {
-  using C = Cfg<PAIR, ATMEM>;
+__global__ void __launch_bounds__(Cfg<PAIR, ATMEM, ATMEM && wide_tiles<TLEN>()>::THREADS, 1)
+    gemm_tc_kernel(GemmArgs g, Sched sc) {
+  using C = Cfg<PAIR, ATMEM, ATMEM && wide_tiles<TLEN>()>;
   constexpr int NST = C::NST;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -583,14 +604,16 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
     // a's warp w writes tensor-memory lanes 32w..32w+31 (its rows)
     if (warp < PROD_A_WARPS)
       produce<true, TLEN, SPD, PAIR, ATMEM>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep, threadIdx.x,
-                                            lane, tmem + ((uint32_t)(32 * warp) << 16) + TMEM_A_COL);
+                                            lane, tmem + ((uint32_t)(32 * warp) << 16) + C::TMEM_A);
     else
       produce<false, TLEN, SPD, PAIR, ATMEM>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep,
                                              threadIdx.x - PROD_A_WARPS * 32, lane, 0u);
   } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer (leader CTA)
     if (lane == 0 && leader) {
-      const uint32_t idesc = C::idesc_n(sc.tile_b);
+      const int nmma = C::WIDE ? 2 : 1;                 // MMAs per K step
+      const int nw = sc.tile_b / nmma;                   // width of each
+      const uint32_t idesc = C::idesc_n(nw);
       uint32_t it = 0, uc = 0;
       for (int w = tile0; w < sc.nwork; w += tstep) {
         const Work wk = work_of(sc, w, g.d);
@@ -612,10 +635,12 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM>::THREADS, 1) gemm_tc_kernel(G
             for (int kk = 0; kk < KS / 32; ++kk) {
               const uint32_t off = (kk & 3) * 32;
               const uint32_t acc = (st > 0 || kk > 0) ? 1u : 0u;
-              if constexpr (ATMEM)
-                mma_i8_ts(tacc, tmem + TMEM_A_COL + s * 64 + kk * 8, smem_desc(b_base + (kk >> 2) * C::B_ATOM + off),
-                          idesc, acc);
-              else
+              if constexpr (ATMEM) {
+#pragma unroll
+                for (int h = 0; h < nmma; ++h)  // half h: columns [h*nw, (h+1)*nw), smem rows from h*nw/2
+                  mma_i8_ts(tacc + h * nw, tmem + C::TMEM_A + s * 64 + kk * 8,
+                            smem_desc(b_base + (kk >> 2) * C::B_ATOM + h * (nw / 2) * 128 + off), idesc, acc);
+              } else
                 mma_i8<PAIR>(tacc, smem_desc(a_base + (kk >> 2) * C::A_ATOM + off),
                              smem_desc(b_base + (kk >> 2) * C::B_ATOM + off), idesc, acc);
             }
@@ -824,7 +849,7 @@ done:
 
 template <int TLEN, int SPD, bool PAIR, bool ATMEM = false>
 static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int sms, cudaStream_t st) {
-  using C = Cfg<PAIR, ATMEM>;
+  using C = Cfg<PAIR, ATMEM, ATMEM && wide_tiles<TLEN>()>;
   static bool attr = false;
   auto kern = gemm_tc_kernel<TLEN, SPD, PAIR, ATMEM>;
   if (!attr) {
@@ -883,6 +908,24 @@ static bool use_pair() {
 // tensor memory (the epilogue is then a visible share of a tile).
 constexpr int kShortTileStages = 512;
 
+// Which kernel a call runs: SM pairs or single SMs (SCMP_TC_SINGLE=1), and on
+// pairs, a in tensor memory with wide tiles when there is one accumulation
+// unit and the tiles are long (SCMP_TC_ASMEM=1 keeps a in shared memory).
+struct Variant {
+  bool pair, atmem, wide;
+};
+static Variant choose_variant(int d, int unit_d, int lp) {
+  Variant v;
+  v.pair = use_pair();
+  const int nunits = cdiv(d, unit_d > 0 ? unit_d : d);
+  const int tlen = lp < 256 ? lp : 256;
+  const int stages = (tlen < 256 ? cdiv(d, 256 / tlen) : d) * (lp / tlen);
+  const char* asmem = getenv("SCMP_TC_ASMEM");
+  v.atmem = v.pair && nunits == 1 && stages >= kShortTileStages && !(asmem && asmem[0] == '1');
+  v.wide = v.atmem && lp < 256;  // wide_tiles<TLEN>()
+  return v;
+}
+
 static int device_sms() {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -901,13 +944,16 @@ constexpr size_t kSplitBudget = 64u << 20;  // bytes of part accumulators, at mo
 // K parts S that minimises the last wave's length, ceil(rem*S/units)/S of a
 // tile, within the limits above (SCMP_TC_NO_SPLIT=1 in the environment turns
 // splitting off).
-static Sched make_sched(int batch, int n, int m, int d, int unit_d, bool pair, int sms) {
+static Sched make_sched(int batch, int n, int m, int d, int unit_d, Variant v, int sms) {
+  const bool pair = v.pair;
   Sched s{};
   s.tile_a = pair ? Cfg<true>::TILE_A : Cfg<false>::TILE_A;
-  // columns per tile: b's rows in equal tiles of at most 256, a multiple of 16
-  // (the MMA's N), so that a small or ragged m does not pay for 256
-  s.tiles_b = cdiv(m, 256);
-  s.tile_b = cdiv(cdiv(m, s.tiles_b), 16) * 16;
+  // columns per tile: b's rows in equal tiles of at most TILE_B, a multiple of
+  // 16 per MMA (N), so that a small or ragged m does not pay for a full tile
+  const int tmax = v.wide ? Cfg<true, true, true>::TILE_B : 256;
+  const int gran = v.wide ? 32 : 16;
+  s.tiles_b = cdiv(m, tmax);
+  s.tile_b = cdiv(cdiv(m, s.tiles_b), gran) * gran;
   s.tiles_a = cdiv(n, s.tile_a);
   s.tiles = batch * s.tiles_a * s.tiles_b;
   s.unit_d = unit_d > 0 ? unit_d : d;
@@ -919,7 +965,7 @@ static Sched make_sched(int batch, int n, int m, int d, int unit_d, bool pair, i
   const int rem = s.tiles % units;
   const char* off = getenv("SCMP_TC_NO_SPLIT");
   if (s.nunits == 1 && rem > 0 && !(off && off[0] == '1')) {
-    const size_t part_bytes = (size_t)(pair ? 2 : 1) * 128 * 256 * sizeof(int);
+    const size_t part_bytes = (size_t)(pair ? 2 : 1) * 128 * (v.wide ? 320 : 256) * sizeof(int);
     double best = 1.0;
     for (int S = 2; S <= kMaxSplit && s.nblk / S >= kMinSplitBlocks; ++S) {
       if ((size_t)rem * S * part_bytes > kSplitBudget) break;
@@ -936,24 +982,26 @@ static Sched make_sched(int batch, int n, int m, int d, int unit_d, bool pair, i
 }
 }  // namespace tc
 
-size_t gemm_tc_split_cnt_offset(int batch, int n, int m, int d, int unit_d) {
-  const bool pair = use_pair();
-  const tc::Sched s = tc::make_sched(batch, n, m, d, unit_d, pair, device_sms());
-  return (size_t)(s.tiles - s.full) * s.split * (pair ? 2 : 1) * 128 * 256 * sizeof(int);
+size_t gemm_tc_split_cnt_offset(int batch, int n, int m, int d, int unit_d, int lp) {
+  const Variant v = choose_variant(d, unit_d, lp);
+  const tc::Sched s = tc::make_sched(batch, n, m, d, unit_d, v, device_sms());
+  return (size_t)(s.tiles - s.full) * s.split * (v.pair ? 2 : 1) * 128 * (v.wide ? 320 : 256) * sizeof(int);
 }
 
-size_t gemm_tc_split_bytes(int batch, int n, int m, int d, int unit_d) {
-  const bool pair = use_pair();
-  const tc::Sched s = tc::make_sched(batch, n, m, d, unit_d, pair, device_sms());
+size_t gemm_tc_split_bytes(int batch, int n, int m, int d, int unit_d, int lp) {
+  const Variant v = choose_variant(d, unit_d, lp);
+  const tc::Sched s = tc::make_sched(batch, n, m, d, unit_d, v, device_sms());
   if (s.split == 1) return 0;
-  return gemm_tc_split_cnt_offset(batch, n, m, d, unit_d) + (size_t)(s.tiles - s.full) * (pair ? 2 : 1) * sizeof(int);
+  return gemm_tc_split_cnt_offset(batch, n, m, d, unit_d, lp) +
+         (size_t)(s.tiles - s.full) * (v.pair ? 2 : 1) * sizeof(int);
 }
 
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
   using namespace tc;
-  const bool pair = use_pair();
+  const Variant v = choose_variant(g.d, g.unit_d, g.lp);
+  const bool pair = v.pair;
   const int sms = device_sms();
-  Sched s = make_sched(g.batch, g.n, g.m, g.d, g.unit_d, pair, sms);
+  Sched s = make_sched(g.batch, g.n, g.m, g.d, g.unit_d, v, sms);
   if (s.split > 1) {
     if (!g.split_acc || !g.split_cnt) {  // no workspace for the parts: whole tiles only
       s.full = s.tiles;
@@ -968,12 +1016,7 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
   const int spd = g.lp / tlen;
   // a in tensor memory needs the running-sum columns free: one accumulation
   // unit per tile (SCMP_TC_ASMEM=1 keeps a in shared memory)
-  // short tiles (few K stages) instead keep a in shared memory, which frees
-  // the tensor-memory columns for a second accumulator: the epilogue of one
-  // tile then overlaps the next tile's MMAs
-  const char* asmem = getenv("SCMP_TC_ASMEM");
-  const int stages_per_tile = (tlen < 256 ? cdiv(g.d, 256 / tlen) : g.d) * spd;
-  if (pair && s.nunits == 1 && stages_per_tile >= kShortTileStages && !(asmem && asmem[0] == '1')) {
+  if (v.atmem) {
     switch (tlen) {
       case 32: return launch_t<32, 1, true, true>(g, s, sms, st);
       case 64: return launch_t<64, 1, true, true>(g, s, sms, st);

@@ -143,7 +143,7 @@ bool gemm_tc_supported(const GemmArgs& g);
 // Workspace of the tcgen05 GEMM's split last wave for this shape on the
 // current device (0 when the last wave is not split); the counters sit at
 // byte offset gemm_tc_split_cnt_offset of that block.
-size_t gemm_tc_split_bytes(int batch, int n, int m, int d, int unit_d);
-size_t gemm_tc_split_cnt_offset(int batch, int n, int m, int d, int unit_d);
+size_t gemm_tc_split_bytes(int batch, int n, int m, int d, int unit_d, int lp);
+size_t gemm_tc_split_cnt_offset(int batch, int n, int m, int d, int unit_d, int lp);
 
 }  // namespace scmp
