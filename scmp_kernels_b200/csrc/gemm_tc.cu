@@ -51,18 +51,22 @@ constexpr int TMEM_COLS = 512;
 template <int TLEN>
 __host__ __device__ constexpr bool wide_tiles() { return TLEN < 256; }
 
+// WIDE without ATMEM (SM pairs, a in shared memory): up to 512 b rows per
+// tile as two MMAs of width 256 that share every a stage; the accumulator
+// takes all 512 tensor-memory columns and two shared-memory stages of
+// 32 + 64 KB are used.
 template <bool PAIR, bool ATMEM = false, bool WIDE_ = false>
 struct Cfg {
   static_assert(PAIR || !ATMEM, "a in tensor memory is implemented for SM pairs");
-  static_assert(ATMEM || !WIDE_, "wide tiles need a in tensor memory");
+  static_assert(PAIR || !WIDE_, "wide tiles are implemented for SM pairs");
   static constexpr bool WIDE = WIDE_;                     // two half-width MMAs per K step
   static constexpr int BM = 128;                          // a rows per CTA
   static constexpr int TILE_A = PAIR ? 256 : 128;         // a rows per tile
-  static constexpr int TILE_B = WIDE ? 320 : 256;         // most b rows per tile; the
+  static constexpr int TILE_B = WIDE ? (ATMEM ? 320 : 512) : 256;  // most b rows per tile; the
                                                           // schedule's tile_b <= TILE_B is used
   static constexpr int BNL = TILE_B / (PAIR ? 2 : 1);     // b rows per CTA
   static constexpr int TMEM_A = TILE_B;                   // first tensor-memory column of a's stages
-  static constexpr int NST = WIDE ? 3 : ATMEM ? 4 : PAIR ? 3 : 2;  // pipeline stages
+  static constexpr int NST = WIDE ? (ATMEM ? 3 : 2) : ATMEM ? 4 : PAIR ? 3 : 2;  // pipeline stages
   static constexpr int A_BYTES = ATMEM ? 0 : BM * KS;     // a's bytes of a smem stage
   static constexpr int B_BYTES = BNL * KS;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -371,11 +375,11 @@ __device__ __forceinline__ int stages_of_unit(int len) {
 // loops); the chunks of a stage are. Returns false after an abort.
 // With ATMEM, side a writes its row's 64 columns of each stage to tensor
 // memory at tmem_a (this thread's lane, first stage column) instead.
-template <bool SIDE_A, int TLEN, int SPD, bool PAIR, bool ATMEM>
+template <bool SIDE_A, int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE>
 __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint32_t sbase, uint32_t bar_base,
                                         volatile int* abort_flag, uint32_t rank, int tile0, int tstep, int r,
                                         int lane, uint32_t tmem_a) {
-  using C = Cfg<PAIR, ATMEM, ATMEM && wide_tiles<TLEN>()>;
+  using C = Cfg<PAIR, ATMEM, WIDE>;
   constexpr int NST = C::NST;
   constexpr int DPS = TLEN < 256 ? 256 / TLEN : 1;
   constexpr int NSPB = SPB<TLEN, SPD>();
@@ -537,10 +541,9 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
 
 // TLEN: padded stream length lp when lp <= 256 (256/lp dimensions per stage),
 // or 256 when lp = 256*SPD (SPD stages per dimension, SPD = 1 or 2).
-template <int TLEN, int SPD, bool PAIR, bool ATMEM>
-__global__ void __launch_bounds__(Cfg<PAIR, ATMEM, ATMEM && wide_tiles<TLEN>()>::THREADS, 1)
-    gemm_tc_kernel(GemmArgs g, Sched sc) {
-  using C = Cfg<PAIR, ATMEM, ATMEM && wide_tiles<TLEN>()>;
+template <int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE>
+__global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched sc) {
+  using C = Cfg<PAIR, ATMEM, WIDE>;
   constexpr int NST = C::NST;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -554,7 +557,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, ATMEM && wide_tiles<TLEN>()>:
   // accumulator buffers: two (tensor-memory columns [0,256) and [256,512))
   // when those columns are free (a in shared memory, one accumulation unit per
   // tile), so that a tile's epilogue overlaps the next tile's MMAs; else one
-  const int nbuf = (!ATMEM && sc.nunits == 1) ? 2 : 1;
+  const int nbuf = (!ATMEM && !WIDE && sc.nunits == 1) ? 2 : 1;
   auto accf_bar = [&](int b) { return bar_base + 8u * (2 * NST + b); };
   auto acce_bar = [&](int b) { return bar_base + 8u * (2 * NST + 2 + b); };
   const uint32_t drain_bar = bar_base + 8u * (2 * NST + 4);
@@ -603,10 +606,10 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, ATMEM && wide_tiles<TLEN>()>:
     // ------------------------------------------------------------ producers
     // a's warp w writes tensor-memory lanes 32w..32w+31 (its rows)
     if (warp < PROD_A_WARPS)
-      produce<true, TLEN, SPD, PAIR, ATMEM>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep, threadIdx.x,
+      produce<true, TLEN, SPD, PAIR, ATMEM, WIDE>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep, threadIdx.x,
                                             lane, tmem + ((uint32_t)(32 * warp) << 16) + C::TMEM_A);
     else
-      produce<false, TLEN, SPD, PAIR, ATMEM>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep,
+      produce<false, TLEN, SPD, PAIR, ATMEM, WIDE>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep,
                                              threadIdx.x - PROD_A_WARPS * 32, lane, 0u);
   } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer (leader CTA)
@@ -640,9 +643,12 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, ATMEM && wide_tiles<TLEN>()>:
                 for (int h = 0; h < nmma; ++h)  // half h: columns [h*nw, (h+1)*nw), smem rows from h*nw/2
                   mma_i8_ts(tacc + h * nw, tmem + C::TMEM_A + s * 64 + kk * 8,
                             smem_desc(b_base + (kk >> 2) * C::B_ATOM + h * (nw / 2) * 128 + off), idesc, acc);
-              } else
-                mma_i8<PAIR>(tacc, smem_desc(a_base + (kk >> 2) * C::A_ATOM + off),
-                             smem_desc(b_base + (kk >> 2) * C::B_ATOM + off), idesc, acc);
+              } else {
+#pragma unroll
+                for (int h = 0; h < nmma; ++h)
+                  mma_i8<PAIR>(tacc + h * nw, smem_desc(a_base + (kk >> 2) * C::A_ATOM + off),
+                               smem_desc(b_base + (kk >> 2) * C::B_ATOM + h * (nw / 2) * 128 + off), idesc, acc);
+              }
             }
             mma_commit<PAIR>(empty_bar(s));
           }
@@ -847,11 +853,11 @@ done:
   }
 }
 
-template <int TLEN, int SPD, bool PAIR, bool ATMEM = false>
+template <int TLEN, int SPD, bool PAIR, bool ATMEM = false, bool WIDE = ATMEM && wide_tiles<TLEN>()>
 static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int sms, cudaStream_t st) {
-  using C = Cfg<PAIR, ATMEM, ATMEM && wide_tiles<TLEN>()>;
+  using C = Cfg<PAIR, ATMEM, WIDE>;
   static bool attr = false;
-  auto kern = gemm_tc_kernel<TLEN, SPD, PAIR, ATMEM>;
+  auto kern = gemm_tc_kernel<TLEN, SPD, PAIR, ATMEM, WIDE>;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
@@ -908,11 +914,17 @@ static bool use_pair() {
 // tensor memory (the epilogue is then a visible share of a tile).
 constexpr int kShortTileStages = 512;
 
-// Which kernel a call runs: SM pairs or single SMs (SCMP_TC_SINGLE=1), and on
-// pairs, a in tensor memory with wide tiles when there is one accumulation
-// unit and the tiles are long (SCMP_TC_ASMEM=1 keeps a in shared memory).
+// Which kernel a call runs. SM pairs (single SMs with SCMP_TC_SINGLE=1);
+// on pairs, with one accumulation unit per tile and long tiles, 512-wide
+// tiles with a in shared memory (SCMP_TC_ATMEM=1 selects a in tensor memory
+// instead, 256- or 320-wide tiles); short tiles use two 256-wide accumulators
+// and the chunked path one accumulator plus the running sum.
+static bool env_on(const char* name) {
+  const char* e = getenv(name);
+  return e && e[0] == '1';
+}
 struct Variant {
-  bool pair, atmem, wide;
+  bool pair, atmem, wide;  // wide without atmem: 512-wide tiles, a in shared memory
 };
 static Variant choose_variant(int d, int unit_d, int lp) {
   Variant v;
@@ -920,9 +932,9 @@ static Variant choose_variant(int d, int unit_d, int lp) {
   const int nunits = cdiv(d, unit_d > 0 ? unit_d : d);
   const int tlen = lp < 256 ? lp : 256;
   const int stages = (tlen < 256 ? cdiv(d, 256 / tlen) : d) * (lp / tlen);
-  const char* asmem = getenv("SCMP_TC_ASMEM");
-  v.atmem = v.pair && nunits == 1 && stages >= kShortTileStages && !(asmem && asmem[0] == '1');
-  v.wide = v.atmem && lp < 256;  // wide_tiles<TLEN>()
+  const bool long_tiles = v.pair && nunits == 1 && stages >= kShortTileStages;
+  v.atmem = long_tiles && env_on("SCMP_TC_ATMEM");
+  v.wide = long_tiles && (!v.atmem || lp < 256);  // wide_tiles<TLEN>() with atmem
   return v;
 }
 
@@ -934,6 +946,10 @@ static int device_sms() {
 }
 
 namespace tc {
+// Columns of a split part's accumulator slot (the variant's most b rows per tile).
+static int tile_cols(const Variant& v) {
+  return v.wide ? (v.atmem ? Cfg<true, true, true>::TILE_B : Cfg<true, false, true>::TILE_B) : 256;
+}
 constexpr int kMaxSplit = 8;              // K parts per tile of the last wave
 constexpr int kMinSplitBlocks = 8;        // blocks of eight dimensions per part, at least
 constexpr size_t kSplitBudget = 64u << 20;  // bytes of part accumulators, at most
@@ -950,7 +966,7 @@ static Sched make_sched(int batch, int n, int m, int d, int unit_d, Variant v, i
   s.tile_a = pair ? Cfg<true>::TILE_A : Cfg<false>::TILE_A;
   // columns per tile: b's rows in equal tiles of at most TILE_B, a multiple of
   // 16 per MMA (N), so that a small or ragged m does not pay for a full tile
-  const int tmax = v.wide ? Cfg<true, true, true>::TILE_B : 256;
+  const int tmax = v.wide ? (v.atmem ? Cfg<true, true, true>::TILE_B : Cfg<true, false, true>::TILE_B) : 256;
   const int gran = v.wide ? 32 : 16;
   s.tiles_b = cdiv(m, tmax);
   s.tile_b = cdiv(cdiv(m, s.tiles_b), gran) * gran;
@@ -965,7 +981,7 @@ static Sched make_sched(int batch, int n, int m, int d, int unit_d, Variant v, i
   const int rem = s.tiles % units;
   const char* off = getenv("SCMP_TC_NO_SPLIT");
   if (s.nunits == 1 && rem > 0 && !(off && off[0] == '1')) {
-    const size_t part_bytes = (size_t)(pair ? 2 : 1) * 128 * (v.wide ? 320 : 256) * sizeof(int);
+    const size_t part_bytes = (size_t)(pair ? 2 : 1) * 128 * tile_cols(v) * sizeof(int);
     double best = 1.0;
     for (int S = 2; S <= kMaxSplit && s.nblk / S >= kMinSplitBlocks; ++S) {
       if ((size_t)rem * S * part_bytes > kSplitBudget) break;
@@ -985,7 +1001,7 @@ static Sched make_sched(int batch, int n, int m, int d, int unit_d, Variant v, i
 size_t gemm_tc_split_cnt_offset(int batch, int n, int m, int d, int unit_d, int lp) {
   const Variant v = choose_variant(d, unit_d, lp);
   const tc::Sched s = tc::make_sched(batch, n, m, d, unit_d, v, device_sms());
-  return (size_t)(s.tiles - s.full) * s.split * (v.pair ? 2 : 1) * 128 * (v.wide ? 320 : 256) * sizeof(int);
+  return (size_t)(s.tiles - s.full) * s.split * (v.pair ? 2 : 1) * 128 * tc::tile_cols(v) * sizeof(int);
 }
 
 size_t gemm_tc_split_bytes(int batch, int n, int m, int d, int unit_d, int lp) {
@@ -1014,8 +1030,16 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
   }
   const int tlen = g.lp < 256 ? g.lp : 256;
   const int spd = g.lp / tlen;
-  // a in tensor memory needs the running-sum columns free: one accumulation
-  // unit per tile (SCMP_TC_ASMEM=1 keeps a in shared memory)
+  if (v.wide && !v.atmem) {  // 512-wide tiles, a in shared memory (default for long tiles)
+    switch (tlen) {
+      case 32: return launch_t<32, 1, true, false, true>(g, s, sms, st);
+      case 64: return launch_t<64, 1, true, false, true>(g, s, sms, st);
+      case 128: return launch_t<128, 1, true, false, true>(g, s, sms, st);
+      default:
+        return spd == 2 ? launch_t<256, 2, true, false, true>(g, s, sms, st)
+                        : launch_t<256, 1, true, false, true>(g, s, sms, st);
+    }
+  }
   if (v.atmem) {
     switch (tlen) {
       case 32: return launch_t<32, 1, true, true>(g, s, sms, st);

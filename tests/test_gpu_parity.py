@@ -28,13 +28,13 @@ from scmp_kernels_b200.sc import kernels as K  # noqa: E402
 DEV = "cuda:0"
 
 
-@pytest.fixture(params=["tc2", "tc2smem", "tc1", "simt"])
+@pytest.fixture(params=["tc2", "tc2atmem", "tc1", "simt"])
 def impl(request, monkeypatch):
-    """tc2: tcgen05 on SM pairs, a in tensor memory where the path allows
-    (default); tc2smem: SM pairs with a in shared memory; tc1: tcgen05 on
-    single SMs; simt: CUDA cores."""
+    """tc2: tcgen05 on SM pairs (default: 512-wide tiles for long tiles, two
+    accumulators for short ones); tc2atmem: SM pairs with a in tensor memory
+    for long tiles; tc1: tcgen05 on single SMs; simt: CUDA cores."""
     monkeypatch.setattr(K, "_FORCE_SIMT", request.param == "simt")
-    monkeypatch.setenv("SCMP_TC_ASMEM", "1" if request.param == "tc2smem" else "0")
+    monkeypatch.setenv("SCMP_TC_ATMEM", "1" if request.param == "tc2atmem" else "0")
     if request.param == "tc1":
         monkeypatch.setenv("SCMP_TC_SINGLE", "1")
     else:
@@ -139,12 +139,11 @@ def test_tc_variants_match_simt_at_size(shape, kw, monkeypatch, env_vars):
     a = torch.randn(n, d, device=DEV, generator=g)
     b = torch.randn(m, d, device=DEV, generator=g) * 0.02
     outs = []
-    # CUDA cores; SM pairs (a in tensor memory unless chunked); SM pairs with a
-    # in shared memory; single SMs
-    for simt, single, asmem in ((True, "0", "0"), (False, "0", "0"), (False, "0", "1"), (False, "1", "0")):
+    # CUDA cores; SM pairs (default); SM pairs with a in tensor memory; single SMs
+    for simt, single, atmem in ((True, "0", "0"), (False, "0", "0"), (False, "0", "1"), (False, "1", "0")):
         monkeypatch.setattr(K, "_FORCE_SIMT", simt)
         monkeypatch.setenv("SCMP_TC_SINGLE", single)
-        monkeypatch.setenv("SCMP_TC_ASMEM", asmem)
+        monkeypatch.setenv("SCMP_TC_ATMEM", atmem)
         outs.append(sc_matmul(a, b, **kw))
     for i, o in enumerate(outs[1:], 1):
         assert torch.equal(outs[0], o), f"variant {i} differs from the CUDA-core GEMM"
@@ -247,8 +246,8 @@ def test_native_kernels_do_the_work():
 def test_full_size_workloads_agree_across_gemm_variants(workload, rows, monkeypatch, env_vars):
     """The benchmark workloads at their full sizes (config 5: its first 512
     rows of a against all of b; per_row quantisation is row-local, so a row
-    slice is an exact sub-problem): the default GEMM (SM pairs, a in tensor
-    memory, split last wave), SM pairs with a in shared memory, and the
+    slice is an exact sub-problem): the default GEMM (SM pairs, 512-wide
+    tiles, split last wave), SM pairs with a in tensor memory, and the
     CUDA-core GEMM give the same bits, and every output is finite."""
     env_vars({})
     from scmp_kernels_b200 import workloads as W
@@ -264,9 +263,9 @@ def test_full_size_workloads_agree_across_gemm_variants(workload, rows, monkeypa
         a, b = (q, k) if workload == "config3qk" else (probs, v_t)
         kw = dict(granularity="per_head", sc_prec=8)
     outs = []
-    for simt, asmem in ((False, "0"), (False, "1"), (True, "0")):
+    for simt, atmem in ((False, "0"), (False, "1"), (True, "0")):
         monkeypatch.setattr(K, "_FORCE_SIMT", simt)
-        monkeypatch.setenv("SCMP_TC_ASMEM", asmem)
+        monkeypatch.setenv("SCMP_TC_ATMEM", atmem)
         outs.append(sc_matmul(a, b, **kw))
     assert torch.isfinite(outs[0]).all()
     for i, o in enumerate(outs[1:], 1):
