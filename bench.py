@@ -38,11 +38,12 @@ WORKLOADS = {
 }
 
 
-# DRAM bytes of one GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum)
-# from an ncu capture of the 2048-row case of the config-2 recipe (539.2 MB,
-# profiles/gemm_tc_pair_tmemA_2048x11008x4096.md), scaled to the 4096 rows of
-# the full workload: the a rows and the bands of a that re-read b both double.
-GEMM_TRAFFIC_BYTES = {"config2": 2 * 539.2e6}
+# DRAM bytes of one GEMM launch (DRAM read + write bytes) from an ncu capture of
+# the 2048-row case of the config-2 recipe (370.6 MB,
+# profiles/gemm_tc_pair_wide512_2048x11008x4096.md), scaled to the 4096 rows of
+# the full workload: the a rows, the output and the bands of a that re-read b
+# all double.
+GEMM_TRAFFIC_BYTES = {"config2": 2 * 370.6e6}
 
 
 def parse():

@@ -83,7 +83,6 @@ struct Cfg {
   static constexpr int SB_BYTES = TILE_B * 4;            // a chunk's column scales (chunked path)
   static constexpr int SMEM_BYTES = NST * STAGE_BYTES + STG_BYTES + SB_BYTES + 1024 + 256;
   static constexpr int NCTA = PAIR ? 2 : 1;
-  // kind::i8, D = s32, A = B = s8, K-major; N = 256, M = 128 per SM
   // kind::i8, D = s32, A = B = s8, K-major, M = 128 per SM; N from idesc_n()
   static constexpr uint32_t IDESC_M = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)((PAIR ? 256 : 128) >> 4) << 24);
   __device__ static uint32_t idesc_n(int n) { return IDESC_M | ((uint32_t)(n >> 3) << 17); }
@@ -261,33 +260,63 @@ __device__ __forceinline__ void store_rows32(const GemmArgs& g, uint32_t stg, in
 
 struct Sched {
   int tiles, tiles_a, tiles_b, nunits, unit_d, tile_a, tile_b;
-  int full, split, nwork, nblk;
+  int full;     // whole tiles, taken round-robin by the workers (a multiple of `workers` with a tail)
+  int workers;  // workers of the persistent grid (SM pairs or SMs)
+  int tail_w;   // workers sharing the tail tiles' K range (0: no tail)
+  int tail_blk; // blocks of eight dimensions in the tail: (tiles - full) * nblk
+  int nwork, nblk;
 };
 
+// Work items of a worker: whole tiles w = worker, worker + workers, ... < full,
+// then (with a tail) its two tail pieces w = full + worker + j * workers. The
+// tail is the last `tiles - full` tiles' K ranges laid end to end (tile after
+// tile, blocks of eight dimensions) and cut into tail_w equal ranges, one per
+// worker ("stream-K"), so every worker ends at the same time; a range spans at
+// most two tiles, piece j of the worker being its part in the j-th of them.
 struct Work {
   int tile;  // output tile
-  int part;  // K part of a split tile, -1 for a whole tile
-  int d0, d1;  // dimension range of a part
+  int part;  // slot of a tail piece (2 * worker + j), -1 for a whole tile
+  int d0, d1;  // dimension range of a piece (d0 == d1: no work)
 };
+
+__host__ __device__ __forceinline__ int tail_lo(const Sched& s, int u) {  // first block of worker u's range
+  return (int)((long long)u * s.tail_blk / s.tail_w);
+}
+// Worker whose range holds tail block x: the largest u with tail_lo(u) <= x.
+__host__ __device__ __forceinline__ int tail_worker(const Sched& s, int x) {
+  return (int)(((long long)(x + 1) * s.tail_w - 1) / s.tail_blk);
+}
 
 __device__ __forceinline__ Work work_of(const Sched& s, int w, int d) {
   Work k;
-  if (w < s.full) {
-    k.tile = w;
-    k.part = -1;
-    k.d0 = 0;
-    k.d1 = d;
-  } else {
+  k.tile = w;
+  k.part = -1;
+  k.d0 = 0;
+  k.d1 = d;
+  if (w >= s.full) {
     const int v = w - s.full;
-    k.tile = s.full + v / s.split;
-    k.part = v % s.split;
-    k.d0 = 8 * (int)((long long)k.part * s.nblk / s.split);
-    k.d1 = min(8 * (int)((long long)(k.part + 1) * s.nblk / s.split), d);
+    const int u = v % s.workers, j = v / s.workers;
+    k.part = 2 * u + j;
+    k.tile = s.full;
+    k.d0 = k.d1 = 0;
+    if (u < s.tail_w) {
+      const int lo = tail_lo(s, u), hi = tail_lo(s, u + 1);
+      const int t = lo / s.nblk + j;  // tail tile of piece j
+      const int b0 = j == 0 ? lo : t * s.nblk;
+      const int b1 = min(hi, (t + 1) * s.nblk);
+      if (b1 > b0) {
+        k.tile = s.full + t;
+        k.d0 = 8 * (b0 - t * s.nblk);
+        k.d1 = min(8 * (b1 - t * s.nblk), d);
+      }
+    }
   }
   return k;
 }
 // Accumulation units of a work item and the dimension range of unit u.
-__device__ __forceinline__ int units_of(const Sched& s, const Work& k) { return k.part < 0 ? s.nunits : 1; }
+__device__ __forceinline__ int units_of(const Sched& s, const Work& k) {
+  return k.part < 0 ? s.nunits : (k.d1 > k.d0 ? 1 : 0);
+}
 __device__ __forceinline__ void unit_range(const Sched& s, const Work& k, int u, int d, int& d0, int& d1) {
   if (k.part < 0) {
     d0 = u * s.unit_d;
@@ -678,12 +707,13 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
     uint32_t uc = 0;
     for (int w = tile0; w < sc.nwork; w += tstep) {
       const Work wk = work_of(sc, w, g.d);
+      if (units_of(sc, wk) == 0) continue;  // empty tail piece
       int bh, a0, b0;
       tile_coords(sc, wk.tile, bh, a0, b0);
       const int ia = a0 + (int)rank * C::BM + 32 * q + lane;
       const int m_end = min(g.m, b0 + sc.tile_b);  // end of this tile's columns
       if (wk.part >= 0) {
-        // ---- one K part of a split tile
+        // ---- one K piece of a tail tile
         const int buf = (int)(uc % nbuf);
         if (!mbar_wait(accf_bar(buf), (uc / nbuf) & 1, abort_flag, 5)) goto done;
         ++uc;
@@ -692,7 +722,9 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
         const int st = wk.tile - sc.full;
         const size_t slot_ints = (size_t)C::BM * C::TILE_B;
         const int rowq = 32 * q + lane;
-        int* mine = g.split_acc + ((size_t)(st * sc.split + wk.part) * C::NCTA + rank) * slot_ints;
+        int* mine = g.split_acc + ((size_t)wk.part * C::NCTA + rank) * slot_ints;
+        // the tile's pieces: those of the workers whose ranges meet its blocks
+        const int u_first = tail_worker(sc, st * sc.nblk), u_last = tail_worker(sc, (st + 1) * sc.nblk - 1);
 #pragma unroll 1
         for (int cb = 0; cb < cdiv(sc.tile_b, 16); ++cb) {
           uint32_t acc[16];
@@ -706,7 +738,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
         __threadfence();
         asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
         if (warp == C::EPI_WARP0 && lane == 0)
-          *split_flag = atomicAdd(g.split_cnt + st * C::NCTA + rank, 1) == sc.split - 1;
+          *split_flag = atomicAdd(g.split_cnt + st * C::NCTA + rank, 1) == u_last - u_first;
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (*split_flag) {
           // last part to finish: the other parts' accumulators are complete
@@ -720,11 +752,12 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
               uint32_t acc[16];
               TMEM_LD16(acc_addr + cb * 16, acc);
               tmem_wait_ld();
-              for (int p = 0; p < sc.split; ++p) {
+              for (int u = u_first; u <= u_last; ++u) {
+                // a worker that starts in an earlier tile has its second piece here
+                const int p = 2 * u + (tail_lo(sc, u) < st * sc.nblk ? 1 : 0);
                 if (p == wk.part) continue;
                 const int4* src = reinterpret_cast<const int4*>(
-                    g.split_acc + ((size_t)(st * sc.split + p) * C::NCTA + rank) * slot_ints +
-                    ((size_t)cb * C::BM + rowq) * 16);
+                    g.split_acc + ((size_t)p * C::NCTA + rank) * slot_ints + ((size_t)cb * C::BM + rowq) * 16);
 #pragma unroll
                 for (int x = 0; x < 4; ++x) {
                   const int4 v = __ldcg(src + x);
@@ -864,12 +897,12 @@ static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int sms, cudaStre
     attr = true;
   }
   if constexpr (!PAIR) {
-    const int grid = s.nwork < sms ? s.nwork : sms;
+    const int grid = s.workers;
     kern<<<grid, C::THREADS, C::SMEM_BYTES, st>>>(g, s);
     count_launch();
     return cudaGetLastError();
   } else {
-    const int pairs = s.nwork < sms / 2 ? s.nwork : sms / 2;
+    const int pairs = s.workers;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
     cfg.blockDim = dim3(C::THREADS, 1, 1);
@@ -950,23 +983,23 @@ namespace tc {
 static int tile_cols(const Variant& v) {
   return v.wide ? (v.atmem ? Cfg<true, true, true>::TILE_B : Cfg<true, false, true>::TILE_B) : 256;
 }
-constexpr int kMaxSplit = 8;              // K parts per tile of the last wave
-constexpr int kMinSplitBlocks = 8;        // blocks of eight dimensions per part, at least
-constexpr size_t kSplitBudget = 64u << 20;  // bytes of part accumulators, at most
+constexpr int kMaxSplit = 8;              // tail pieces per tile, about, at most
+constexpr int kMinSplitBlocks = 8;        // blocks of eight dimensions per tail range, at least
+constexpr size_t kSplitBudget = 128u << 20;  // bytes of tail-piece accumulators, at most
 
-// Schedule of the persistent grid: `units` workers (SM pairs or SMs) take
-// whole tiles round-robin; when the tiles leave a last wave of `rem` < units
-// tiles (and d is one accumulation unit), those are split into the number of
-// K parts S that minimises the last wave's length, ceil(rem*S/units)/S of a
-// tile, within the limits above (SCMP_TC_NO_SPLIT=1 in the environment turns
-// splitting off).
+// Schedule of the persistent grid: the workers (SM pairs or SMs) take whole
+// tiles round-robin; when that leaves a last wave of rem < workers tiles (and
+// d is one accumulation unit), the rem tiles' K ranges are shared evenly by
+// tail_w workers (work_of), so the last wave takes rem / tail_w of a tile
+// instead of a whole one. tail_w is the number of workers, within the limits
+// above (SCMP_TC_NO_SPLIT=1 in the environment turns the tail off).
 static Sched make_sched(int batch, int n, int m, int d, int unit_d, Variant v, int sms) {
   const bool pair = v.pair;
   Sched s{};
   s.tile_a = pair ? Cfg<true>::TILE_A : Cfg<false>::TILE_A;
   // columns per tile: b's rows in equal tiles of at most TILE_B, a multiple of
   // 16 per MMA (N), so that a small or ragged m does not pay for a full tile
-  const int tmax = v.wide ? (v.atmem ? Cfg<true, true, true>::TILE_B : Cfg<true, false, true>::TILE_B) : 256;
+  const int tmax = tile_cols(v);
   const int gran = v.wide ? 32 : 16;
   s.tiles_b = cdiv(m, tmax);
   s.tile_b = cdiv(cdiv(m, s.tiles_b), gran) * gran;
@@ -976,38 +1009,41 @@ static Sched make_sched(int batch, int n, int m, int d, int unit_d, Variant v, i
   s.nunits = cdiv(d, s.unit_d);
   s.nblk = cdiv(d, 8);
   s.full = s.tiles;
-  s.split = 1;
   const int units = pair ? sms / 2 : sms;
+  s.workers = s.tiles < units ? s.tiles : units;
   const int rem = s.tiles % units;
   const char* off = getenv("SCMP_TC_NO_SPLIT");
   if (s.nunits == 1 && rem > 0 && !(off && off[0] == '1')) {
-    const size_t part_bytes = (size_t)(pair ? 2 : 1) * 128 * tile_cols(v) * sizeof(int);
-    double best = 1.0;
-    for (int S = 2; S <= kMaxSplit && s.nblk / S >= kMinSplitBlocks; ++S) {
-      if ((size_t)rem * S * part_bytes > kSplitBudget) break;
-      const double len = (double)cdiv(rem * S, units) / S;
-      if (len < best - 1e-9) {
-        best = len;
-        s.split = S;
-      }
+    const size_t part_bytes = (size_t)(pair ? 2 : 1) * 128 * tmax * sizeof(int);
+    const long long tblk = (long long)rem * s.nblk;
+    long long tw = units;
+    if (tw > (long long)rem * kMaxSplit) tw = (long long)rem * kMaxSplit;
+    if (tw > tblk / kMinSplitBlocks) tw = tblk / kMinSplitBlocks;
+    if (tw > (long long)(kSplitBudget / (2 * part_bytes))) tw = (long long)(kSplitBudget / (2 * part_bytes));
+    if (tw > rem) {  // each worker's share is less than one tile
+      s.full = s.tiles - rem;
+      s.workers = units;
+      s.tail_w = (int)tw;
+      s.tail_blk = (int)tblk;
     }
-    if (s.split > 1) s.full = s.tiles - rem;
   }
-  s.nwork = s.full + (s.tiles - s.full) * s.split;
+  s.nwork = s.full + (s.tail_w > 0 ? 2 * s.workers : 0);
   return s;
 }
 }  // namespace tc
 
+// Workspace of the tail: 2 * tail_w piece accumulators (slot 2u + j: worker u's
+// piece j), then one arrival counter per tail tile and CTA.
 size_t gemm_tc_split_cnt_offset(int batch, int n, int m, int d, int unit_d, int lp) {
   const Variant v = choose_variant(d, unit_d, lp);
   const tc::Sched s = tc::make_sched(batch, n, m, d, unit_d, v, device_sms());
-  return (size_t)(s.tiles - s.full) * s.split * (v.pair ? 2 : 1) * 128 * tc::tile_cols(v) * sizeof(int);
+  return (size_t)2 * s.tail_w * (v.pair ? 2 : 1) * 128 * tc::tile_cols(v) * sizeof(int);
 }
 
 size_t gemm_tc_split_bytes(int batch, int n, int m, int d, int unit_d, int lp) {
   const Variant v = choose_variant(d, unit_d, lp);
   const tc::Sched s = tc::make_sched(batch, n, m, d, unit_d, v, device_sms());
-  if (s.split == 1) return 0;
+  if (s.tail_w == 0) return 0;
   return gemm_tc_split_cnt_offset(batch, n, m, d, unit_d, lp) +
          (size_t)(s.tiles - s.full) * (v.pair ? 2 : 1) * sizeof(int);
 }
@@ -1018,10 +1054,10 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
   const bool pair = v.pair;
   const int sms = device_sms();
   Sched s = make_sched(g.batch, g.n, g.m, g.d, g.unit_d, v, sms);
-  if (s.split > 1) {
-    if (!g.split_acc || !g.split_cnt) {  // no workspace for the parts: whole tiles only
+  if (s.tail_w > 0) {
+    if (!g.split_acc || !g.split_cnt) {  // no workspace for the pieces: whole tiles only
       s.full = s.tiles;
-      s.split = 1;
+      s.tail_w = 0;
       s.nwork = s.tiles;
     } else {
       const cudaError_t e = cudaMemsetAsync(g.split_cnt, 0, (size_t)(s.tiles - s.full) * (pair ? 2 : 1) * sizeof(int), st);

@@ -151,14 +151,17 @@ def test_tc_variants_match_simt_at_size(shape, kw, monkeypatch, env_vars):
 
 
 @pytest.mark.parametrize("shape,kw", [
-    ((1000, 5000, 512), dict(granularity="per_row", sc_prec=8)),                 # 80 tiles: 1 wave + 6
-    ((600, 300, 1000), dict(granularity="per_tensor", mode="unipolar", sc_prec=7)),  # 6 tiles, all split
+    ((1000, 5000, 512), dict(granularity="per_row", sc_prec=8)),                 # fewer tiles than workers
+    ((2048, 11008, 1024), dict(granularity="per_row", sc_prec=8)),               # 2 waves + a 28-tile tail
+    ((600, 300, 1000), dict(granularity="per_tensor", mode="unipolar", sc_prec=7)),  # 6 tiles, all shared
     ((9, 197, 197, 640), dict(granularity="per_head", sc_prec=8)),                 # 9 heads, one tile each
+    ((300, 700, 40), dict(granularity="per_row", sc_prec=8)),                    # 5 blocks: no tail
 ])
 @pytest.mark.parametrize("single", ["0", "1"])
 def test_split_last_wave_matches_whole_tiles(shape, kw, single, monkeypatch, env_vars):
-    """Tiles of the last wave split over K (part accumulators summed by the
-    last part to finish) give the same bits as whole tiles."""
+    """The last wave's tiles shared over K by all workers (pieces of uneven
+    length, a worker's range spanning two tiles, the pieces' accumulators
+    summed by the last to finish) give the same bits as whole tiles."""
     env_vars({})
     g = torch.Generator(device=DEV).manual_seed(5)
     if len(shape) == 4:
