@@ -74,8 +74,13 @@ struct Cfg {
   static constexpr int B_ATOM = BNL * 128;
   static constexpr int PROD_B_WARPS = BNL / 32;
   static constexpr int PROD_WARPS = PROD_A_WARPS + PROD_B_WARPS;
+  // With one accumulator (wide tiles) the MMAs and the epilogue of a tile never
+  // overlap, so the first epilogue warp's lane 0 (leader CTA) issues the MMAs:
+  // one warp fewer leaves more registers per thread (the block's warps are
+  // allocated registers in groups of four).
+  static constexpr bool MERGED = WIDE;
   static constexpr int MMA_WARP = PROD_WARPS;
-  static constexpr int EPI_WARP0 = MMA_WARP + 1;
+  static constexpr int EPI_WARP0 = MERGED ? MMA_WARP : MMA_WARP + 1;
   static constexpr int NWARPS = EPI_WARP0 + 4;
   static constexpr int THREADS = NWARPS * 32;
   // epilogue staging: 4 warps x 32 rows x 32 result columns (float32)
@@ -631,6 +636,58 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // MMAs of accumulation unit u of work item wk into accumulator buffer uc % nbuf
+  // (leader CTA, one thread); it counts the K stages consumed. False on abort.
+  auto issue_unit = [&](const Work& wk, int u, uint32_t& it, uint32_t uc) -> bool {
+    const int nmma = C::WIDE ? 2 : 1;  // MMAs per K step
+    const int nw = sc.tile_b / nmma;   // width of each
+    const uint32_t idesc = C::idesc_n(nw);
+    const int buf = (int)(uc % nbuf);
+    if (!mbar_wait(acce_bar(buf), ((uc / nbuf) & 1) ^ 1, abort_flag, 4)) return false;
+    const uint32_t tacc = tmem + (uint32_t)buf * 256;
+    tc_fence_after();
+    int d0, d1;
+    unit_range(sc, wk, u, g.d, d0, d1);
+    const int nst = stages_of_unit<TLEN>(d1 - d0) * SPD;
+    for (int st = 0; st < nst; ++st, ++it) {
+      const int s = it % NST;
+      if (!mbar_wait(full_bar(s), (it / NST) & 1, abort_flag, 3)) return false;
+      tc_fence_after();
+      const uint32_t a_base = sbase + s * C::STAGE_BYTES, b_base = a_base + C::A_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < KS / 32; ++kk) {
+        const uint32_t off = (kk & 3) * 32;
+        const uint32_t acc = (st > 0 || kk > 0) ? 1u : 0u;
+        if constexpr (ATMEM) {
+#pragma unroll
+          for (int h = 0; h < nmma; ++h)  // half h: columns [h*nw, (h+1)*nw), smem rows from h*nw/2
+            mma_i8_ts(tacc + h * nw, tmem + C::TMEM_A + s * 64 + kk * 8,
+                      smem_desc(b_base + (kk >> 2) * C::B_ATOM + h * (nw / 2) * 128 + off), idesc, acc);
+        } else {
+#pragma unroll
+          for (int h = 0; h < nmma; ++h)
+            mma_i8<PAIR>(tacc + h * nw, smem_desc(a_base + (kk >> 2) * C::A_ATOM + off),
+                         smem_desc(b_base + (kk >> 2) * C::B_ATOM + h * (nw / 2) * 128 + off), idesc, acc);
+        }
+      }
+      mma_commit<PAIR>(empty_bar(s));
+    }
+    mma_commit<PAIR>(accf_bar(buf));
+    return true;
+  };
+  // Completes once every MMA issued before has finished; waited on even after
+  // an abort, so tensor memory is never freed under a live MMA.
+  auto drain = [&]() {
+    if constexpr (PAIR) {
+      asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(drain_bar)
+                   : "memory");
+    } else {
+      mma_commit<false>(drain_bar);
+    }
+    int zero = 0;
+    mbar_wait(drain_bar, 0, &zero, 6);
+  };
+
   if (warp < C::PROD_WARPS) {
     // ------------------------------------------------------------ producers
     // a's warp w writes tensor-memory lanes 32w..32w+31 (its rows)
@@ -640,74 +697,37 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
     else
       produce<false, TLEN, SPD, PAIR, ATMEM, WIDE>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep,
                                              threadIdx.x - PROD_A_WARPS * 32, lane, 0u);
-  } else if (warp == C::MMA_WARP) {
+  } else if (!C::MERGED && warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer (leader CTA)
     if (lane == 0 && leader) {
-      const int nmma = C::WIDE ? 2 : 1;                 // MMAs per K step
-      const int nw = sc.tile_b / nmma;                   // width of each
-      const uint32_t idesc = C::idesc_n(nw);
       uint32_t it = 0, uc = 0;
       for (int w = tile0; w < sc.nwork; w += tstep) {
         const Work wk = work_of(sc, w, g.d);
         const int nu = units_of(sc, wk);
-        for (int u = 0; u < nu; ++u, ++uc) {
-          const int buf = (int)(uc % nbuf);
-          if (!mbar_wait(acce_bar(buf), ((uc / nbuf) & 1) ^ 1, abort_flag, 4)) goto mma_done;
-          const uint32_t tacc = tmem + (uint32_t)buf * 256;
-          tc_fence_after();
-          int d0, d1;
-          unit_range(sc, wk, u, g.d, d0, d1);
-          const int nst = stages_of_unit<TLEN>(d1 - d0) * SPD;
-          for (int st = 0; st < nst; ++st, ++it) {
-            const int s = it % NST;
-            if (!mbar_wait(full_bar(s), (it / NST) & 1, abort_flag, 3)) goto mma_done;
-            tc_fence_after();
-            const uint32_t a_base = sbase + s * C::STAGE_BYTES, b_base = a_base + C::A_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < KS / 32; ++kk) {
-              const uint32_t off = (kk & 3) * 32;
-              const uint32_t acc = (st > 0 || kk > 0) ? 1u : 0u;
-              if constexpr (ATMEM) {
-#pragma unroll
-                for (int h = 0; h < nmma; ++h)  // half h: columns [h*nw, (h+1)*nw), smem rows from h*nw/2
-                  mma_i8_ts(tacc + h * nw, tmem + C::TMEM_A + s * 64 + kk * 8,
-                            smem_desc(b_base + (kk >> 2) * C::B_ATOM + h * (nw / 2) * 128 + off), idesc, acc);
-              } else {
-#pragma unroll
-                for (int h = 0; h < nmma; ++h)
-                  mma_i8<PAIR>(tacc + h * nw, smem_desc(a_base + (kk >> 2) * C::A_ATOM + off),
-                               smem_desc(b_base + (kk >> 2) * C::B_ATOM + h * (nw / 2) * 128 + off), idesc, acc);
-              }
-            }
-            mma_commit<PAIR>(empty_bar(s));
-          }
-          mma_commit<PAIR>(accf_bar(buf));
-        }
+        for (int u = 0; u < nu; ++u, ++uc)
+          if (!issue_unit(wk, u, it, uc)) goto mma_done;
       }
     mma_done:
-      // drain: completes once every MMA issued above has finished; waited on
-      // even after an abort, so tensor memory is never freed under a live MMA
-      if constexpr (PAIR) {
-        asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(drain_bar)
-                     : "memory");
-      } else {
-        mma_commit<false>(drain_bar);
-      }
-      {
-        int zero = 0;
-        mbar_wait(drain_bar, 0, &zero, 6);
-      }
+      drain();
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
+    // (MERGED: the first epilogue warp's lane 0 in the leader CTA issues each
+    // work item's MMAs before the warp turns to that item's epilogue)
+    const bool issuer = C::MERGED && warp == C::MMA_WARP && leader;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16);
     const uint32_t stg = stg_base + (uint32_t)q * (32 * 32 * 4);  // this warp's staging area
-    uint32_t uc = 0;
+    uint32_t uc = 0, mit = 0;
     for (int w = tile0; w < sc.nwork; w += tstep) {
       const Work wk = work_of(sc, w, g.d);
       if (units_of(sc, wk) == 0) continue;  // empty tail piece
+      if (issuer) {  // one accumulation unit per item with wide tiles
+        int ok = 1;
+        if (lane == 0) ok = issue_unit(wk, 0, mit, uc) ? 1 : 0;
+        if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) goto epi_out;
+      }
       int bh, a0, b0;
       tile_coords(sc, wk.tile, bh, a0, b0);
       const int ia = a0 + (int)rank * C::BM + 32 * q + lane;
@@ -715,7 +735,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
       if (wk.part >= 0) {
         // ---- one K piece of a tail tile
         const int buf = (int)(uc % nbuf);
-        if (!mbar_wait(accf_bar(buf), (uc / nbuf) & 1, abort_flag, 5)) goto done;
+        if (!mbar_wait(accf_bar(buf), (uc / nbuf) & 1, abort_flag, 5)) goto epi_out;
         ++uc;
         tc_fence_after();
         const uint32_t acc_addr = lane_addr + (uint32_t)buf * 256;
@@ -787,7 +807,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
       const bool chunked = g.epi.kind == EPI_CHUNK;
       for (int u = 0; u < sc.nunits; ++u, ++uc) {
         const int buf = (int)(uc % nbuf);
-        if (!mbar_wait(accf_bar(buf), (uc / nbuf) & 1, abort_flag, 5)) goto done;
+        if (!mbar_wait(accf_bar(buf), (uc / nbuf) & 1, abort_flag, 5)) goto epi_out;
         tc_fence_after();
         const uint32_t acc_addr = lane_addr + (uint32_t)buf * 256;  // running sum: lane_addr + 256
         const bool last = u == sc.nunits - 1;
@@ -869,8 +889,10 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
         if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar(buf), rank);
       }
     }
+  epi_out:
+    if (issuer && lane == 0) drain();
+    __syncwarp();
   }
-done:
   tc_fence_before();
   __syncthreads();
   if constexpr (PAIR) cluster_sync();  // no CTA leaves while its peer may still touch it
