@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define SCMP_ABI_VERSION 2
+#define SCMP_ABI_VERSION 3
 
 enum scmp_status {
   SCMP_OK = 0,
@@ -67,13 +67,19 @@ enum scmp_mode { SCMP_BIPOLAR = 0, SCMP_UNIPOLAR = 1 };
  *            order: position 32w + 16h + 4q + i at bit 8i + 4h + q (h < 2,
  *            q, i < 4), so that one shift and one mask of a word yield four
  *            consecutive positions as the bytes of an int8 operand word.
+ *   pattern4: NULL, or the same streams with position 32w + 8q + i (q < 4,
+ *            i < 8) at bit 4i + q of word w ("e2m1-sliced"), so that one
+ *            shift and one mask yield eight consecutive positions as the
+ *            nibbles of a 4-bit (e2m1) operand word. Passing it to
+ *            scmp_sc_matmul lets the GEMM run on e2m1 operands
+ *            (tcgen05.mma.kind::mxf4, twice the int8 rate; same results).
  * lp >= L is the padded stream length (a multiple of 32). Every sequence value
  * must be < vcap, so that boundaries >= vcap saturate (ktab = L, all bits set).
  * The reference's cum_indicator[d][k][v] equals the number of set positions t < k of
  * pattern[d][v].
  */
 int scmp_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, int n_rb, int L, int lp,
-                      int vcap, int16_t* ktab, uint32_t* pattern, void* stream);
+                      int vcap, int16_t* ktab, uint32_t* pattern, uint32_t* pattern4, void* stream);
 
 /*
  * One sc_matmul call: quantise both operands, run the integer SC-GEMM and the
@@ -131,6 +137,7 @@ typedef struct scmp_matmul_desc {
   int n_out_peers;         /* 0 .. SCMP_MAX_OUT_PEERS                              */
   int out_ld;              /* row stride of the destinations, >= m                */
   long long out_offset;    /* element offset of (0, 0, 0) in every destination    */
+  const uint32_t* pattern4; /* from scmp_build_tables, or NULL (int8 operands)     */
 } scmp_matmul_desc;
 
 #define SCMP_MAX_OUT_PEERS 8

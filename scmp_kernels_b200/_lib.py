@@ -26,7 +26,7 @@ PER_TENSOR, PER_ROW, PER_HEAD = 0, 1, 2
 BIPOLAR, UNIPOLAR = 0, 1
 FLAG_FORCE_SIMT = 0x1
 FLAG_NO_SPLIT = 0x2
-ABI_VERSION = 2
+ABI_VERSION = 3
 MAX_OUT_PEERS = 8
 
 c_int, c_void_p, c_size_t, c_float, c_double = (ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
@@ -43,6 +43,7 @@ class MatmulDesc(ctypes.Structure):
         ("ktab", c_void_p), ("pattern", c_void_p), ("amap", c_void_p), ("bmap", c_void_p),
         ("vcap", c_int), ("lp", c_int), ("flags", c_int), ("tensor_ranges", c_void_p),
         ("out_peers", c_void_p), ("n_out_peers", c_int), ("out_ld", c_int), ("out_offset", ctypes.c_longlong),
+        ("pattern4", c_void_p),
     ]
 
 
@@ -54,7 +55,7 @@ SIGNATURES = {
     "scmp_last_error": (ctypes.c_char_p, []),
     "scmp_device_error": (c_int, [ctypes.POINTER(c_int)]),
     "scmp_build_tables": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
-                                  c_void_p, c_void_p]),
+                                  c_void_p, c_void_p, c_void_p]),
     "scmp_peer_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p), c_void_p]),
     "scmp_peer_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
     "scmp_peer_close": (c_int, [c_void_p]),

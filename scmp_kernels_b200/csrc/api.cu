@@ -136,13 +136,14 @@ static void carve(const scmp_matmul_desc* d, Carver& c, Plan& p) {
   p.scal = c.take<float>(8);
   if (!(d->flags & (SCMP_FLAG_FORCE_SIMT | SCMP_FLAG_NO_SPLIT))) {
     const int unit_d = p.chunked ? d->chunk_d : d->d;
-    const size_t bytes = gemm_tc_split_bytes(d->batch, d->n, d->m, d->d, unit_d, d->lp);
+    const bool f4 = d->pattern4 != nullptr;
+    const size_t bytes = gemm_tc_split_bytes(d->batch, d->n, d->m, d->d, unit_d, d->lp, f4);
     if (bytes) {
       char* blk = c.take<char>(bytes);
       if (blk) {
         p.split_acc = reinterpret_cast<int*>(blk);
         p.split_cnt =
-            reinterpret_cast<int*>(blk + gemm_tc_split_cnt_offset(d->batch, d->n, d->m, d->d, unit_d, d->lp));
+            reinterpret_cast<int*>(blk + gemm_tc_split_cnt_offset(d->batch, d->n, d->m, d->d, unit_d, d->lp, f4));
       }
     }
   }
@@ -200,12 +201,12 @@ int scmp_device_error(int* code) {
 }
 
 int scmp_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, int n_rb, int L, int lp,
-                      int vcap, int16_t* ktab, uint32_t* pattern, void* stream) {
+                      int vcap, int16_t* ktab, uint32_t* pattern, uint32_t* pattern4, void* stream) {
   if (L < 1 || lp < L || lp % 32 || vcap < 1 || vcap > 32767 || n_ra < 0 || n_rb < 0)
     return fail(SCMP_ERR_INVALID_ARG, "build_tables: bad sizes");
   if ((n_ra && (!ra || !ktab)) || (n_rb && (!rb || !pattern)))
     return fail(SCMP_ERR_INVALID_ARG, "build_tables: null pointer");
-  SCMP_CUDA(launch_build_tables(ra, n_ra, rb, n_rb, L, lp, vcap, ktab, pattern,
+  SCMP_CUDA(launch_build_tables(ra, n_ra, rb, n_rb, L, lp, vcap, ktab, pattern, pattern4,
                                 (cudaStream_t)stream),
             "build_tables");
   return SCMP_OK;
@@ -292,6 +293,7 @@ int scmp_sc_matmul(const scmp_matmul_desc* d, void* workspace, size_t workspace_
   g.ka = p.ka;
   g.vb = p.vb;
   g.pattern = d->pattern;
+  g.pattern4 = d->pattern4;
   g.bmap = p.bmap;
   SCMP_CUDA(launch_pad_map(d->bmap, d->d, p.bmap, st), "pad bmap");
   g.unit_d = d->d;

@@ -55,15 +55,31 @@ __host__ __device__ constexpr bool wide_tiles() { return TLEN < 256; }
 // tile as two MMAs of width 256 that share every a stage; the accumulator
 // takes all 512 tensor-memory columns and two shared-memory stages of
 // 32 + 64 KB are used.
-template <bool PAIR, bool ATMEM = false, bool WIDE_ = false>
+//
+// F4 (SM pairs, a in shared memory): the operands are e2m1 (4-bit) values
+// 0, +1, -1 and the MMA is tcgen05.mma.kind::mxf4 with every block scale 1.0
+// (E8M0 0x7F), twice the int8 MMA rate; its float32 accumulator holds the
+// integer sums exactly (|S| <= D * L < 2^24). A 256-byte stage carries 512 K
+// positions. The scale factors sit in tensor-memory columns
+// [F4_SF_COL, F4_SF_COL + 16), so the accumulator takes at most 480 columns:
+// tiles of at most 480 (wide) or 240 b rows, while shared memory and the
+// producer warps stay sized for 512 / 256 rows (rows past the tile are not
+// read by the MMA).
+constexpr int F4_SF_COL = 480;
+template <bool PAIR, bool ATMEM = false, bool WIDE_ = false, bool F4_ = false>
 struct Cfg {
   static_assert(PAIR || !ATMEM, "a in tensor memory is implemented for SM pairs");
   static_assert(PAIR || !WIDE_, "wide tiles are implemented for SM pairs");
+  static_assert(!F4_ || (PAIR && !ATMEM), "e2m1 operands are implemented for SM pairs with a in shared memory");
   static constexpr bool WIDE = WIDE_;                     // two half-width MMAs per K step
+  static constexpr bool F4 = F4_;                         // e2m1 operands, kind::mxf4
   static constexpr int BM = 128;                          // a rows per CTA
   static constexpr int TILE_A = PAIR ? 256 : 128;         // a rows per tile
-  static constexpr int TILE_B = WIDE ? (ATMEM ? 320 : 512) : 256;  // most b rows per tile; the
-                                                          // schedule's tile_b <= TILE_B is used
+  static constexpr int TILE_B = WIDE ? (ATMEM ? 320 : 512) : 256;  // b rows per tile the shared
+                                                          // memory and producers are sized for
+  static constexpr int TILE_MAX = F4 ? (WIDE ? 480 : 240) : TILE_B;  // most b rows per tile; the
+                                                          // schedule's tile_b <= TILE_MAX is used
+  static constexpr int ACC_STRIDE = F4 ? 240 : 256;       // columns between accumulator buffers
   static constexpr int BNL = TILE_B / (PAIR ? 2 : 1);     // b rows per CTA
   static constexpr int TMEM_A = TILE_B;                   // first tensor-memory column of a's stages
   static constexpr int NST = WIDE ? (ATMEM ? 3 : 2) : ATMEM ? 4 : PAIR ? 3 : 2;  // pipeline stages
@@ -88,10 +104,24 @@ struct Cfg {
   static constexpr int SB_BYTES = TILE_B * 4;            // a chunk's column scales (chunked path)
   static constexpr int SMEM_BYTES = NST * STAGE_BYTES + STG_BYTES + SB_BYTES + 1024 + 256;
   static constexpr int NCTA = PAIR ? 2 : 1;
-  // kind::i8, D = s32, A = B = s8, K-major, M = 128 per SM; N from idesc_n()
-  static constexpr uint32_t IDESC_M = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)((PAIR ? 256 : 128) >> 4) << 24);
+  // kind::i8, D = s32, A = B = s8, K-major, M = 128 per SM; N from idesc_n().
+  // kind::mxf4: A = B = E2M1, scale factors E8M0, K-major, K = 64, scale
+  // factor ids 0; N from idesc_n().
+  static constexpr uint32_t IDESC_M =
+      F4 ? ((1u << 7) | (1u << 10) | (1u << 23) | ((uint32_t)((PAIR ? 256 : 128) >> 4) << 24))
+         : ((2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)((PAIR ? 256 : 128) >> 4) << 24));
   __device__ static uint32_t idesc_n(int n) { return IDESC_M | ((uint32_t)(n >> 3) << 17); }
 };
+
+// Positions of the stream per 256-byte stage (one byte per int8 value, half a
+// byte per e2m1 value) and the dimensions a stage covers for padded stream
+// length TLEN (TLEN = 256 * SPD covers one dimension in SPD stages).
+template <bool F4>
+__host__ __device__ constexpr int stage_positions() { return F4 ? 512 : 256; }
+template <int TLEN, bool F4>
+__host__ __device__ constexpr int dims_per_stage() {
+  return TLEN < stage_positions<F4>() ? stage_positions<F4>() / TLEN : 1;
+}
 
 // Shared-memory matrix descriptor, K-major with 128-byte swizzle: rows at a
 // 128-byte pitch, 8-row groups 1024 bytes apart (SBO), version 1.
@@ -138,6 +168,28 @@ __device__ __forceinline__ void mma_i8_ts(uint32_t tmem_d, uint32_t tmem_a, uint
       "tcgen05.mma.cta_group::2.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
       "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc)
       : "memory");
+}
+// kind::mxf4 MMA (M = 256 over the pair or 128, N from idesc, K = 64) with
+// both operands in shared memory and the scale factors of a and b at
+// tensor-memory address sf (all 1.0).
+template <bool PAIR>
+__device__ __forceinline__ void mma_f4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t acc, uint32_t sf) {
+  if constexpr (PAIR) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%5], p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(sf)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%5], p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(sf)
+        : "memory");
+  }
 }
 // Arrive on `bar` (same offset) in every CTA of the tile once all MMAs issued
 // so far by this thread have completed.
@@ -210,12 +262,6 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Persistent schedule over work items. Items 0..full-1 are whole tiles
-// 0..full-1 (all accumulation units); the remaining tiles full..tiles-1 (the
-// last, partial wave) are each split into `split` parts over contiguous ranges
-// of blocks of eight dimensions, so that the last wave keeps every SM pair
-// busy. A part stores its integer accumulator and the last part of a tile to
-// finish (a per-tile counter) adds the others' and runs the epilogue.
 __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
@@ -261,6 +307,14 @@ __device__ __forceinline__ void store_rows32(const GemmArgs& g, uint32_t stg, in
     }
   }
   __syncwarp();
+}
+
+// Integer value of an accumulator word: int32 for kind::i8, a float32 holding
+// an integer below 2^24 in magnitude for kind::mxf4 (exact conversion).
+template <bool F4>
+__device__ __forceinline__ int acc_int(uint32_t w) {
+  if constexpr (F4) return __float2int_rz(__uint_as_float(w));
+  return (int)w;
 }
 
 struct Sched {
@@ -340,9 +394,9 @@ __device__ __forceinline__ void tile_coords(const Sched& s, int tile, int& bh, i
   b0 = (r % s.tiles_b) * s.tile_b;
 }
 
-template <int TLEN, int SPD>
+template <int TLEN, int SPD, bool F4 = false>
 __host__ __device__ constexpr int SPB() {  // stages per block of eight dimensions
-  return (TLEN < 256 ? 8 / (256 / TLEN) : 8) * SPD;
+  return (8 / dims_per_stage<TLEN, F4>()) * SPD;
 }
 
 // Signed value of dimension e (0..7, compile-time after unrolling) of a block.
@@ -355,31 +409,34 @@ __device__ __forceinline__ int bm_at(const int4& lo, const int4& hi, int e) {
        : e == 4 ? hi.x : e == 5 ? hi.y : e == 6 ? hi.z : hi.w;
 }
 
-// The 8 stream words (256 bits) that stage j of a block expands: for each of
-// its DPS dimensions, TLEN bits of the row (bmap, |v|), starting at bit
-// (j % SPD) * TLEN. Dimensions past d1, empty rows and v == 0 give zeros.
-template <int TLEN, int SPD>
-__device__ __forceinline__ void load_stream_words(const GemmArgs& g, const uint4& kv, const int4& bl,
-                                                  const int4& bh, int j, int dbase, int d1, bool valid,
-                                                  uint32_t LW, uint32_t (&pw)[8]) {
-  constexpr int DPS = TLEN < 256 ? 256 / TLEN : 1;
-  constexpr int NW = TLEN / 32;
+// The stream words that stage j of a block expands (8 for int8 operands, 16
+// for e2m1): for each of its DPS dimensions, TLEN bits of the row (bmap, |v|)
+// of `pat`, starting at bit (j % SPD) * TLEN. Dimensions past d1, empty rows
+// and v == 0 give zeros.
+template <int TLEN, int SPD, bool F4 = false>
+__device__ __forceinline__ void load_stream_words(const GemmArgs& g, const uint32_t* __restrict__ pat,
+                                                  const uint4& kv, const int4& bl, const int4& bh, int j,
+                                                  int dbase, int d1, bool valid, uint32_t LW,
+                                                  uint32_t (&pw)[F4 ? 16 : 8]) {
+  constexpr int DPS = dims_per_stage<TLEN, F4>();
+  constexpr int NW = TLEN / 32 < 16 ? TLEN / 32 : 16;  // words of one dimension in the stage
+  static_assert(DPS * NW == (F4 ? 16 : 8), "a stage is 8 (int8) or 16 (e2m1) stream words");
 #pragma unroll
   for (int dl = 0; dl < DPS; ++dl) {
     const int e = (j / SPD) * DPS + dl;
     const int v = kv_at(kv, e);
     const int mag = v < 0 ? -v : v;
     if (valid && dbase + e < d1 && mag != 0) {
-      const uint32_t* p = g.pattern + ((size_t)bm_at(bl, bh, e) * (g.vcap + 1) + mag) * LW +
-                          (j % SPD) * NW;
-      if constexpr (NW == 8) {
-        const uint4 x = __ldg(reinterpret_cast<const uint4*>(p));
-        const uint4 y = __ldg(reinterpret_cast<const uint4*>(p) + 1);
-        pw[0] = x.x; pw[1] = x.y; pw[2] = x.z; pw[3] = x.w;
-        pw[4] = y.x; pw[5] = y.y; pw[6] = y.z; pw[7] = y.w;
-      } else if constexpr (NW == 4) {
-        const uint4 x = __ldg(reinterpret_cast<const uint4*>(p));
-        pw[dl * 4 + 0] = x.x; pw[dl * 4 + 1] = x.y; pw[dl * 4 + 2] = x.z; pw[dl * 4 + 3] = x.w;
+      const uint32_t* p = pat + ((size_t)bm_at(bl, bh, e) * (g.vcap + 1) + mag) * LW + (j % SPD) * NW;
+      if constexpr (NW >= 4) {
+#pragma unroll
+        for (int x = 0; x < NW / 4; ++x) {
+          const uint4 y = __ldg(reinterpret_cast<const uint4*>(p) + x);
+          pw[dl * NW + 4 * x] = y.x;
+          pw[dl * NW + 4 * x + 1] = y.y;
+          pw[dl * NW + 4 * x + 2] = y.z;
+          pw[dl * NW + 4 * x + 3] = y.w;
+        }
       } else if constexpr (NW == 2) {
         const uint2 x = __ldg(reinterpret_cast<const uint2*>(p));
         pw[dl * 2] = x.x;
@@ -394,10 +451,10 @@ __device__ __forceinline__ void load_stream_words(const GemmArgs& g, const uint4
   }
 }
 
-template <int TLEN>
+template <int TLEN, bool F4 = false>
 __device__ __forceinline__ int stages_of_unit(int len) {
-  if (TLEN < 256) return cdiv(len, 256 / TLEN);
-  return len * (TLEN / 256);
+  if (TLEN < stage_positions<F4>()) return cdiv(len, dims_per_stage<TLEN, F4>());
+  return len * (TLEN / stage_positions<F4>());
 }
 
 // Producer loop of one operand side. Operands arrive in blocks of eight
@@ -409,14 +466,20 @@ __device__ __forceinline__ int stages_of_unit(int len) {
 // loops); the chunks of a stage are. Returns false after an abort.
 // With ATMEM, side a writes its row's 64 columns of each stage to tensor
 // memory at tmem_a (this thread's lane, first stage column) instead.
-template <bool SIDE_A, int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE>
+// With F4 the words are e2m1: eight 4-bit values (0, +1 = 0x2, -1 = 0xA) per
+// 32-bit word, so a 16-byte chunk covers 32 positions instead of 16.
+template <bool SIDE_A, int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE, bool F4>
 __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint32_t sbase, uint32_t bar_base,
                                         volatile int* abort_flag, uint32_t rank, int tile0, int tstep, int r,
                                         int lane, uint32_t tmem_a) {
-  using C = Cfg<PAIR, ATMEM, WIDE>;
+  using C = Cfg<PAIR, ATMEM, WIDE, F4>;
   constexpr int NST = C::NST;
-  constexpr int DPS = TLEN < 256 ? 256 / TLEN : 1;
-  constexpr int NSPB = SPB<TLEN, SPD>();
+  constexpr int DPS = dims_per_stage<TLEN, F4>();
+  constexpr int NSPB = SPB<TLEN, SPD, F4>();
+  constexpr int NPW = F4 ? 16 : 8;  // stream words per stage
+  // 16-byte chunks of one dimension in a stage
+  constexpr int CPDS = (TLEN < stage_positions<F4>() ? TLEN : stage_positions<F4>()) / (F4 ? 32 : 16);
+  const uint32_t* __restrict__ pat = F4 ? g.pattern4 : g.pattern;
   const int R = SIDE_A ? g.batch * g.n : g.batch * g.m;
   const uint4* kvsrc = reinterpret_cast<const uint4*>(SIDE_A ? g.ka : g.vb);
   const int4* bmsrc = reinterpret_cast<const int4*>(g.bmap);
@@ -448,16 +511,16 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
     for (int u = 0; u < nu; ++u) {
       int d0, d1;
       unit_range(sc, wk, u, g.d, d0, d1);
-      const int nst = stages_of_unit<TLEN>(d1 - d0) * SPD;
+      const int nst = stages_of_unit<TLEN, F4>(d1 - d0) * SPD;
       const int nblk = cdiv(d1 - d0, 8);
       const int blk0 = d0 >> 3;
       uint4 kv_cur = valid ? __ldg(kvsrc + (size_t)blk0 * R + grow) : make_uint4(0, 0, 0, 0);
       int4 bm_lo = make_int4(0, 0, 0, 0), bm_hi = make_int4(0, 0, 0, 0);
-      uint32_t pw[8];
+      uint32_t pw[NPW];
       if (!SIDE_A) {
         bm_lo = __ldg(bmsrc + 2 * blk0);
         bm_hi = __ldg(bmsrc + 2 * blk0 + 1);
-        load_stream_words<TLEN, SPD>(g, kv_cur, bm_lo, bm_hi, 0, d0, d1, valid, LW, pw);
+        load_stream_words<TLEN, SPD, F4>(g, pat, kv_cur, bm_lo, bm_hi, 0, d0, d1, valid, LW, pw);
       }
       for (int blk = 0; blk < nblk; ++blk) {
         const int dbase = d0 + 8 * blk;
@@ -474,12 +537,13 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
         const int jmax = min(NSPB, nst - blk * NSPB);
 #pragma unroll 1
         for (int j = 0; j < jmax; ++j) {
-          uint32_t pn[8];
+          uint32_t pn[NPW];
           if (!SIDE_A) {
             if (j + 1 < NSPB)
-              load_stream_words<TLEN, SPD>(g, kv_cur, bm_lo, bm_hi, j + 1, dbase, d1, valid, LW, pn);
+              load_stream_words<TLEN, SPD, F4>(g, pat, kv_cur, bm_lo, bm_hi, j + 1, dbase, d1, valid, LW, pn);
             else
-              load_stream_words<TLEN, SPD>(g, kv_nxt, nb_lo, nb_hi, 0, dbase + 8, more ? d1 : dbase, valid, LW, pn);
+              load_stream_words<TLEN, SPD, F4>(g, pat, kv_nxt, nb_lo, nb_hi, 0, dbase + 8, more ? d1 : dbase, valid,
+                                               LW, pn);
           }
           const int s = it % NST;
           if (!mbar_wait(bar_base + 8u * (NST + s), ((it / NST) & 1) ^ 1, abort_flag, SIDE_A ? 1 : 2))
@@ -522,31 +586,47 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
               const int kv = (dbase + e < d1) ? kv_at(kv_cur, e) : 0;
               const int mag = kv < 0 ? -kv : kv;
               if (SIDE_A) {
-                // word x of the piece holds positions 4x..4x+3: its low
-                // clamp(mag - tbase - 4x, 0, 4) bytes are `fill`, i.e. the top
-                // bytes of (0:fill) << max(8*(mag - tbase) - 32x, 0), clamped at 32
-                const uint32_t fill = kv < 0 ? 0xFFFFFFFFu : 0x01010101u;
-                const int sh = 8 * (mag - tbase);
+                // word x of the piece holds positions PW*x .. PW*x+PW-1 (PW =
+                // 4 int8 or 8 e2m1 values): its low clamp(mag - tbase - PW*x,
+                // 0, PW) values are `fill`, i.e. the top bits of
+                // (0:fill) << max(VB*(mag - tbase) - 32x, 0) (VB bits per
+                // value), the shift clamped at 32
+                const uint32_t fill = F4 ? (kv < 0 ? 0xAAAAAAAAu : 0x22222222u) : (kv < 0 ? 0xFFFFFFFFu : 0x01010101u);
+                const int sh = (F4 ? 4 : 8) * (mag - tbase);
 #pragma unroll
-                for (int c = 0; c < TLEN / 16; ++c) {
+                for (int c = 0; c < CPDS; ++c) {
                   uint32_t w[4];
 #pragma unroll
                   for (int q = 0; q < 4; ++q)
                     w[q] = __funnelshift_lc(fill, 0u, (uint32_t)max(sh - 32 * (4 * c + q), 0));
-                  const int kc = dl * (TLEN / 16) + c;
+                  const int kc = dl * CPDS + c;
                   st_shared_v4(stage + (kc >> 3) * C::A_ATOM + xo[kc & 7], w[0], w[1], w[2], w[3]);
+                }
+              } else if constexpr (F4) {
+                // e2m1 sliced stream words: chunk c is stream word c of the
+                // dimension; its word q holds nibble-spaced bits q, q+4, ...
+                // (positions 8q .. 8q+7), times 0x2 (+1) or 0xA (-1)
+                const uint32_t mult = kv < 0 ? 0xAu : 0x2u;
+#pragma unroll
+                for (int c = 0; c < CPDS; ++c) {
+                  const uint32_t sw = pw[dl * CPDS + c];
+                  uint32_t w[4];
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) w[q] = ((sw >> q) & 0x11111111u) * mult;
+                  const int kc = dl * CPDS + c;
+                  st_shared_v4(stage + (kc >> 3) * C::B_ATOM + xo[kc & 7], w[0], w[1], w[2], w[3]);
                 }
               } else {
                 // sliced stream words: chunk c's four words are the bytes'
                 // bit 0 of (word >> (4*(c&1) + q)), negated for v < 0
                 const uint32_t mult = kv < 0 ? 0xFFu : 1u;
 #pragma unroll
-                for (int c = 0; c < TLEN / 16; ++c) {
+                for (int c = 0; c < CPDS; ++c) {
                   const uint32_t sw = pw[dl * (TLEN / 32) + (c >> 1)];
                   uint32_t w[4];
 #pragma unroll
                   for (int q = 0; q < 4; ++q) w[q] = ((sw >> (4 * (c & 1) + q)) & 0x01010101u) * mult;
-                  const int kc = dl * (TLEN / 16) + c;
+                  const int kc = dl * CPDS + c;
                   st_shared_v4(stage + (kc >> 3) * C::B_ATOM + xo[kc & 7], w[0], w[1], w[2], w[3]);
                 }
               }
@@ -560,7 +640,7 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
           ++it;
           if (!SIDE_A) {
 #pragma unroll
-            for (int x = 0; x < 8; ++x) pw[x] = pn[x];
+            for (int x = 0; x < NPW; ++x) pw[x] = pn[x];
           }
         }
         kv_cur = kv_nxt;
@@ -575,9 +655,9 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
 
 // TLEN: padded stream length lp when lp <= 256 (256/lp dimensions per stage),
 // or 256 when lp = 256*SPD (SPD stages per dimension, SPD = 1 or 2).
-template <int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE>
-__global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched sc) {
-  using C = Cfg<PAIR, ATMEM, WIDE>;
+template <int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE, bool F4>
+__global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched sc) {
+  using C = Cfg<PAIR, ATMEM, WIDE, F4>;
   constexpr int NST = C::NST;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -635,6 +715,22 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
   if constexpr (PAIR) cluster_sync();  // the peer's barriers exist before anyone arrives on them
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if constexpr (F4) {
+    // block scale factors of every MMA: E8M0 0x7F (2^0) in columns
+    // [F4_SF_COL, F4_SF_COL + 16) of all 128 lanes, in both CTAs of a pair
+    // (an MMA of N <= 256 reads 4 columns for a and 8 for b)
+    if (warp < 4) {
+      const uint32_t one[8] = {0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu,
+                               0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu};
+      TMEM_ST8(tmem + ((uint32_t)(32 * warp) << 16) + F4_SF_COL, one);
+      TMEM_ST8(tmem + ((uint32_t)(32 * warp) << 16) + F4_SF_COL + 8, one);
+      tmem_wait_st();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if constexpr (PAIR) cluster_sync();
+    tc_fence_after();
+  }
 
   // MMAs of accumulation unit u of work item wk into accumulator buffer uc % nbuf
   // (leader CTA, one thread); it counts the K stages consumed. False on abort.
@@ -644,11 +740,11 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
     const uint32_t idesc = C::idesc_n(nw);
     const int buf = (int)(uc % nbuf);
     if (!mbar_wait(acce_bar(buf), ((uc / nbuf) & 1) ^ 1, abort_flag, 4)) return false;
-    const uint32_t tacc = tmem + (uint32_t)buf * 256;
+    const uint32_t tacc = tmem + (uint32_t)(buf * C::ACC_STRIDE);
     tc_fence_after();
     int d0, d1;
     unit_range(sc, wk, u, g.d, d0, d1);
-    const int nst = stages_of_unit<TLEN>(d1 - d0) * SPD;
+    const int nst = stages_of_unit<TLEN, F4>(d1 - d0) * SPD;
     for (int st = 0; st < nst; ++st, ++it) {
       const int s = it % NST;
       if (!mbar_wait(full_bar(s), (it / NST) & 1, abort_flag, 3)) return false;
@@ -663,6 +759,12 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
           for (int h = 0; h < nmma; ++h)  // half h: columns [h*nw, (h+1)*nw), smem rows from h*nw/2
             mma_i8_ts(tacc + h * nw, tmem + C::TMEM_A + s * 64 + kk * 8,
                       smem_desc(b_base + (kk >> 2) * C::B_ATOM + h * (nw / 2) * 128 + off), idesc, acc);
+        } else if constexpr (F4) {
+#pragma unroll
+          for (int h = 0; h < nmma; ++h)
+            mma_f4<PAIR>(tacc + h * nw, smem_desc(a_base + (kk >> 2) * C::A_ATOM + off),
+                         smem_desc(b_base + (kk >> 2) * C::B_ATOM + h * (nw / 2) * 128 + off), idesc, acc,
+                         tmem + F4_SF_COL);
         } else {
 #pragma unroll
           for (int h = 0; h < nmma; ++h)
@@ -692,10 +794,10 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
     // ------------------------------------------------------------ producers
     // a's warp w writes tensor-memory lanes 32w..32w+31 (its rows)
     if (warp < PROD_A_WARPS)
-      produce<true, TLEN, SPD, PAIR, ATMEM, WIDE>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep, threadIdx.x,
+      produce<true, TLEN, SPD, PAIR, ATMEM, WIDE, F4>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep, threadIdx.x,
                                             lane, tmem + ((uint32_t)(32 * warp) << 16) + C::TMEM_A);
     else
-      produce<false, TLEN, SPD, PAIR, ATMEM, WIDE>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep,
+      produce<false, TLEN, SPD, PAIR, ATMEM, WIDE, F4>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep,
                                              threadIdx.x - PROD_A_WARPS * 32, lane, 0u);
   } else if (!C::MERGED && warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer (leader CTA)
@@ -738,9 +840,9 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
         if (!mbar_wait(accf_bar(buf), (uc / nbuf) & 1, abort_flag, 5)) goto epi_out;
         ++uc;
         tc_fence_after();
-        const uint32_t acc_addr = lane_addr + (uint32_t)buf * 256;
+        const uint32_t acc_addr = lane_addr + (uint32_t)(buf * C::ACC_STRIDE);
         const int st = wk.tile - sc.full;
-        const size_t slot_ints = (size_t)C::BM * C::TILE_B;
+        const size_t slot_ints = (size_t)C::BM * C::TILE_MAX;
         const int rowq = 32 * q + lane;
         int* mine = g.split_acc + ((size_t)wk.part * C::NCTA + rank) * slot_ints;
         // the tile's pieces: those of the workers whose ranges meet its blocks
@@ -753,7 +855,8 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
           int4* dst = reinterpret_cast<int4*>(mine + ((size_t)cb * C::BM + rowq) * 16);
 #pragma unroll
           for (int x = 0; x < 4; ++x)
-            dst[x] = make_int4((int)acc[4 * x], (int)acc[4 * x + 1], (int)acc[4 * x + 2], (int)acc[4 * x + 3]);
+            dst[x] = make_int4(acc_int<F4>(acc[4 * x]), acc_int<F4>(acc[4 * x + 1]), acc_int<F4>(acc[4 * x + 2]),
+                               acc_int<F4>(acc[4 * x + 3]));
         }
         __threadfence();
         asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
@@ -772,6 +875,8 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
               uint32_t acc[16];
               TMEM_LD16(acc_addr + cb * 16, acc);
               tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 16; ++j) acc[j] = (uint32_t)acc_int<F4>(acc[j]);
               for (int u = u_first; u <= u_last; ++u) {
                 // a worker that starts in an earlier tile has its second piece here
                 const int p = 2 * u + (tail_lo(sc, u) < st * sc.nblk ? 1 : 0);
@@ -809,7 +914,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
         const int buf = (int)(uc % nbuf);
         if (!mbar_wait(accf_bar(buf), (uc / nbuf) & 1, abort_flag, 5)) goto epi_out;
         tc_fence_after();
-        const uint32_t acc_addr = lane_addr + (uint32_t)buf * 256;  // running sum: lane_addr + 256
+        const uint32_t acc_addr = lane_addr + (uint32_t)(buf * C::ACC_STRIDE);  // running sum: lane_addr + ACC_STRIDE
         const bool last = u == sc.nunits - 1;
         if (chunked && !last) {
           // Chunk u of several: add its scaled values to the running sum in
@@ -830,19 +935,19 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
               const int ib = b0 + cb * 8 + j;
               float x = 0.f;
               if (ia < g.n && ib < m_end)
-                x = fmul(fmul((float)(int)acc[j], g.epi.inner), fmul(sar, sbs[cb * 8 + j]));
+                x = fmul(fmul((float)acc_int<F4>(acc[j]), g.epi.inner), fmul(sar, sbs[cb * 8 + j]));
               acc[j] = __float_as_uint(fadd(u > 0 ? __uint_as_float(run[j]) : 0.f, x));
             }
-            TMEM_ST8(lane_addr + 256 + cb * 8, acc);
+            TMEM_ST8(lane_addr + C::ACC_STRIDE + cb * 8, acc);
           };
           TMEM_LD8(acc_addr, acc0);
-          if (u > 0) TMEM_LD8(lane_addr + 256, run0);
+          if (u > 0) TMEM_LD8(lane_addr + C::ACC_STRIDE, run0);
 #pragma unroll 1
           for (int cb = 0; cb < ns; cb += 2) {
             tmem_wait_ld();
             if (cb + 1 < ns) {
               TMEM_LD8(acc_addr + (cb + 1) * 8, acc1);
-              if (u > 0) TMEM_LD8(lane_addr + 256 + (cb + 1) * 8, run1);
+              if (u > 0) TMEM_LD8(lane_addr + C::ACC_STRIDE + (cb + 1) * 8, run1);
             }
             chunk_slice(cb, acc0, run0);
             if (cb + 1 < ns) {
@@ -850,7 +955,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
               tmem_wait_st();  // acc0 is about to be reloaded; its store has read it
               if (cb + 2 < ns) {
                 TMEM_LD8(acc_addr + (cb + 2) * 8, acc0);
-                if (u > 0) TMEM_LD8(lane_addr + 256 + (cb + 2) * 8, run0);
+                if (u > 0) TMEM_LD8(lane_addr + C::ACC_STRIDE + (cb + 2) * 8, run0);
               }
               chunk_slice(cb + 1, acc1, run1);
               tmem_wait_st();  // likewise acc1
@@ -870,14 +975,14 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
             const int cb = 2 * cp + h;
             uint32_t acc[16], run[16];
             TMEM_LD16(acc_addr + cb * 16, acc);
-            if (chunked && u > 0) TMEM_LD16(lane_addr + 256 + cb * 16, run);
+            if (chunked && u > 0) TMEM_LD16(lane_addr + C::ACC_STRIDE + cb * 16, run);
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int ib = b0 + cb * 16 + j;
               float v = 0.f;
               if (ia < g.n && ib < m_end)
-                v = epi_value(g.epi, (int)acc[j], bh * g.n + ia, bh * g.m + ib, bh, u, g.n, g.m);
+                v = epi_value(g.epi, acc_int<F4>(acc[j]), bh * g.n + ia, bh * g.m + ib, bh, u, g.n, g.m);
               if (chunked) v = fadd(u > 0 ? __uint_as_float(run[j]) : 0.f, v);
               fin[16 * h + j] = __float_as_uint(v);
             }
@@ -908,11 +1013,11 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE>::THREADS, 1) gemm_tc_ke
   }
 }
 
-template <int TLEN, int SPD, bool PAIR, bool ATMEM = false, bool WIDE = ATMEM && wide_tiles<TLEN>()>
+template <int TLEN, int SPD, bool PAIR, bool ATMEM = false, bool WIDE = ATMEM && wide_tiles<TLEN>(), bool F4 = false>
 static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int sms, cudaStream_t st) {
-  using C = Cfg<PAIR, ATMEM, WIDE>;
+  using C = Cfg<PAIR, ATMEM, WIDE, F4>;
   static bool attr = false;
-  auto kern = gemm_tc_kernel<TLEN, SPD, PAIR, ATMEM, WIDE>;
+  auto kern = gemm_tc_kernel<TLEN, SPD, PAIR, ATMEM, WIDE, F4>;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
@@ -980,8 +1085,13 @@ static bool env_on(const char* name) {
 }
 struct Variant {
   bool pair, atmem, wide;  // wide without atmem: 512-wide tiles, a in shared memory
+  bool f4;                 // e2m1 operands (kind::mxf4)
 };
-static Variant choose_variant(int d, int unit_d, int lp) {
+// f4_table: the call carries the e2m1-sliced stream table. e2m1 operands are
+// used on SM pairs with a in shared memory for streams of 64 to 512
+// positions (a stage then covers at most one block of eight dimensions);
+// SCMP_TC_INT8=1 in the environment keeps int8 operands.
+static Variant choose_variant(int d, int unit_d, int lp, bool f4_table) {
   Variant v;
   v.pair = use_pair();
   const int nunits = cdiv(d, unit_d > 0 ? unit_d : d);
@@ -990,6 +1100,7 @@ static Variant choose_variant(int d, int unit_d, int lp) {
   const bool long_tiles = v.pair && nunits == 1 && stages >= kShortTileStages;
   v.atmem = long_tiles && env_on("SCMP_TC_ATMEM");
   v.wide = long_tiles && (!v.atmem || lp < 256);  // wide_tiles<TLEN>() with atmem
+  v.f4 = f4_table && v.pair && !v.atmem && lp >= 64 && lp <= 512 && !env_on("SCMP_TC_INT8");
   return v;
 }
 
@@ -1003,6 +1114,7 @@ static int device_sms() {
 namespace tc {
 // Columns of a split part's accumulator slot (the variant's most b rows per tile).
 static int tile_cols(const Variant& v) {
+  if (v.f4) return v.wide ? Cfg<true, false, true, true>::TILE_MAX : Cfg<true, false, false, true>::TILE_MAX;
   return v.wide ? (v.atmem ? Cfg<true, true, true>::TILE_B : Cfg<true, false, true>::TILE_B) : 256;
 }
 constexpr int kMaxSplit = 8;              // tail pieces per tile, about, at most
@@ -1056,23 +1168,23 @@ static Sched make_sched(int batch, int n, int m, int d, int unit_d, Variant v, i
 
 // Workspace of the tail: 2 * tail_w piece accumulators (slot 2u + j: worker u's
 // piece j), then one arrival counter per tail tile and CTA.
-size_t gemm_tc_split_cnt_offset(int batch, int n, int m, int d, int unit_d, int lp) {
-  const Variant v = choose_variant(d, unit_d, lp);
+size_t gemm_tc_split_cnt_offset(int batch, int n, int m, int d, int unit_d, int lp, bool f4_table) {
+  const Variant v = choose_variant(d, unit_d, lp, f4_table);
   const tc::Sched s = tc::make_sched(batch, n, m, d, unit_d, v, device_sms());
   return (size_t)2 * s.tail_w * (v.pair ? 2 : 1) * 128 * tc::tile_cols(v) * sizeof(int);
 }
 
-size_t gemm_tc_split_bytes(int batch, int n, int m, int d, int unit_d, int lp) {
-  const Variant v = choose_variant(d, unit_d, lp);
+size_t gemm_tc_split_bytes(int batch, int n, int m, int d, int unit_d, int lp, bool f4_table) {
+  const Variant v = choose_variant(d, unit_d, lp, f4_table);
   const tc::Sched s = tc::make_sched(batch, n, m, d, unit_d, v, device_sms());
   if (s.tail_w == 0) return 0;
-  return gemm_tc_split_cnt_offset(batch, n, m, d, unit_d, lp) +
+  return gemm_tc_split_cnt_offset(batch, n, m, d, unit_d, lp, f4_table) +
          (size_t)(s.tiles - s.full) * (v.pair ? 2 : 1) * sizeof(int);
 }
 
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
   using namespace tc;
-  const Variant v = choose_variant(g.d, g.unit_d, g.lp);
+  const Variant v = choose_variant(g.d, g.unit_d, g.lp, g.pattern4 != nullptr);
   const bool pair = v.pair;
   const int sms = device_sms();
   Sched s = make_sched(g.batch, g.n, g.m, g.d, g.unit_d, v, sms);
@@ -1084,6 +1196,22 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
     } else {
       const cudaError_t e = cudaMemsetAsync(g.split_cnt, 0, (size_t)(s.tiles - s.full) * (pair ? 2 : 1) * sizeof(int), st);
       if (e != cudaSuccess) return e;
+    }
+  }
+  if (v.f4) {  // e2m1 operands: TLEN is the padded stream length, 64 .. 512
+    if (v.wide) {
+      switch (g.lp) {
+        case 64: return launch_t<64, 1, true, false, true, true>(g, s, sms, st);
+        case 128: return launch_t<128, 1, true, false, true, true>(g, s, sms, st);
+        case 256: return launch_t<256, 1, true, false, true, true>(g, s, sms, st);
+        default: return launch_t<512, 1, true, false, true, true>(g, s, sms, st);
+      }
+    }
+    switch (g.lp) {
+      case 64: return launch_t<64, 1, true, false, false, true>(g, s, sms, st);
+      case 128: return launch_t<128, 1, true, false, false, true>(g, s, sms, st);
+      case 256: return launch_t<256, 1, true, false, false, true>(g, s, sms, st);
+      default: return launch_t<512, 1, true, false, false, true>(g, s, sms, st);
     }
   }
   const int tlen = g.lp < 256 ? g.lp : 256;

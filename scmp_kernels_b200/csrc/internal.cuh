@@ -74,6 +74,12 @@ __host__ __device__ __forceinline__ size_t blk_idx(int R, int row, int j) {
   return ((size_t)(j >> 3) * R + row) * 8 + (j & 7);
 }
 
+// Bit order of the e2m1-sliced stream words: position 8q + i of a word
+// (q < 4, i < 8) sits at bit 4i + q, so (word >> q) & 0x11111111 has the eight
+// positions 8q .. 8q+7 as the low bits of its nibbles (one e2m1 operand word
+// after a multiply by 0x2 or 0xA).
+__host__ __device__ constexpr int slice4_bit(int l) { return 4 * (l & 7) + (l >> 3); }
+
 // Bit order of the 32-bit comparator-stream words ("sliced"): stream
 // position 16h + 4q + i of a word (h < 2, q < 4, i < 4) sits at bit
 // 8i + 4h + q, so the four positions 16h+4q .. 16h+4q+3 are bit 0 of the four
@@ -113,6 +119,7 @@ struct GemmArgs {
   const int16_t* ka;
   const int16_t* vb;
   const uint32_t* pattern;
+  const uint32_t* pattern4;  // the same streams in e2m1-sliced order, or NULL
   const int32_t* bmap;
   int unit_d;
   Epilogue epi;
@@ -135,7 +142,7 @@ __device__ __forceinline__ void store_out(const GemmArgs& g, int h, int i, int j
 
 // Host launchers (return cudaError_t of the launch).
 cudaError_t launch_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, int n_rb, int L,
-                                int lp, int vcap, int16_t* ktab, uint32_t* pattern,
+                                int lp, int vcap, int16_t* ktab, uint32_t* pattern, uint32_t* pattern4,
                                 cudaStream_t st);
 cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t st);
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st);
@@ -143,7 +150,8 @@ bool gemm_tc_supported(const GemmArgs& g);
 // Workspace of the tcgen05 GEMM's split last wave for this shape on the
 // current device (0 when the last wave is not split); the counters sit at
 // byte offset gemm_tc_split_cnt_offset of that block.
-size_t gemm_tc_split_bytes(int batch, int n, int m, int d, int unit_d, int lp);
-size_t gemm_tc_split_cnt_offset(int batch, int n, int m, int d, int unit_d, int lp);
+// f4_table: the call carries the e2m1-sliced stream table (pattern4).
+size_t gemm_tc_split_bytes(int batch, int n, int m, int d, int unit_d, int lp, bool f4_table);
+size_t gemm_tc_split_cnt_offset(int batch, int n, int m, int d, int unit_d, int lp, bool f4_table);
 
 }  // namespace scmp

@@ -26,9 +26,10 @@ __global__ void k_table_kernel(const int32_t* __restrict__ ra, int L, int vcap,
   }
 }
 
-// pattern[r][v][w] bit slice_bit(i) = (32w + i < L) && rb[r][32w + i] < v
+// pattern[r][v][w] bit slice_bit(i) = (32w + i < L) && rb[r][32w + i] < v,
+// and the same bit at slice4_bit(i) in pattern4 (when given)
 __global__ void pattern_kernel(const int32_t* __restrict__ rb, int L, int lp, int vcap,
-                               uint32_t* __restrict__ pat) {
+                               uint32_t* __restrict__ pat, uint32_t* __restrict__ pat4) {
   extern __shared__ int32_t srow[];
   const int r = blockIdx.x;
   const int lw = lp / 32;
@@ -37,17 +38,21 @@ __global__ void pattern_kernel(const int32_t* __restrict__ rb, int L, int lp, in
   const int total = (vcap + 1) * lw;
   for (int idx = blockIdx.y * blockDim.x + threadIdx.x; idx < total; idx += gridDim.y * blockDim.x) {
     const int v = idx / lw, w = idx % lw;
-    uint32_t bits = 0;
+    uint32_t bits = 0, bits4 = 0;
     for (int i = 0; i < 32; ++i) {
       const int t = 32 * w + i;
-      if (t < L && srow[t] < v) bits |= 1u << slice_bit(i);
+      if (t < L && srow[t] < v) {
+        bits |= 1u << slice_bit(i);
+        bits4 |= 1u << slice4_bit(i);
+      }
     }
     pat[((size_t)r * (vcap + 1) + v) * lw + w] = bits;
+    if (pat4) pat4[((size_t)r * (vcap + 1) + v) * lw + w] = bits4;
   }
 }
 
 cudaError_t launch_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, int n_rb, int L,
-                                int lp, int vcap, int16_t* ktab, uint32_t* pattern,
+                                int lp, int vcap, int16_t* ktab, uint32_t* pattern, uint32_t* pattern4,
                                 cudaStream_t st) {
   const size_t sm = (size_t)L * sizeof(int32_t);
   if (sm > 48 * 1024) {
@@ -64,7 +69,7 @@ cudaError_t launch_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, 
     const int lw = lp / 32;
     const int ys = cdiv((vcap + 1) * lw, 256);
     dim3 grid(n_rb, ys < 64 ? ys : 64);
-    pattern_kernel<<<grid, 256, sm, st>>>(rb, L, lp, vcap, pattern);
+    pattern_kernel<<<grid, 256, sm, st>>>(rb, L, lp, vcap, pattern, pattern4);
     count_launch();
   }
   return cudaGetLastError();

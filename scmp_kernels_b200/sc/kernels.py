@@ -130,6 +130,7 @@ class EnableTables:
     """Device-resident enable tables of one (config, sc_prec, stoc_len, grid)."""
     ktab: torch.Tensor      # (rows_a, vcap+1) int16
     pattern: torch.Tensor   # (rows_b, vcap+1, lp/32) int32 (bit-packed streams)
+    pattern4: torch.Tensor  # the same streams in the e2m1-sliced bit order
     amap: torch.Tensor      # (config q_e,) int32: dimension -> ktab row
     bmap: torch.Tensor      # (config k_e,) int32: dimension -> pattern row
     L: int
@@ -179,14 +180,17 @@ def build_enable_tables(config: dict, sc_prec: int, device, stoc_len: Optional[i
     ub_t = torch.from_numpy(np.ascontiguousarray(ub, dtype=np.int32)).to(dev)
     ktab = torch.empty((ua.shape[0], vcap + 1), dtype=torch.int16, device=dev)
     pattern = torch.empty((ub.shape[0], vcap + 1, lp // 32), dtype=torch.int32, device=dev)
+    pattern4 = torch.empty_like(pattern)
     with torch.cuda.device(dev):
         _lib.check(_lib.lib().scmp_build_tables(
             ua_t.data_ptr(), ua.shape[0], ub_t.data_ptr(), ub.shape[0], stoc_len, lp, vcap,
-            ktab.data_ptr(), pattern.data_ptr(), ctypes.c_void_p(_lib.stream_handle(dev))),
+            ktab.data_ptr(), pattern.data_ptr(), pattern4.data_ptr(),
+            ctypes.c_void_p(_lib.stream_handle(dev))),
             "build_enable_tables")
     amap = torch.from_numpy(np.asarray(ia, dtype=np.int32).reshape(-1)).to(dev)
     bmap = torch.from_numpy(np.asarray(ib, dtype=np.int32).reshape(-1)).to(dev)
-    return EnableTables(ktab, pattern, amap, bmap, stoc_len, lp, G, vcap, min(ra.shape[0], rb.shape[0]))
+    return EnableTables(ktab, pattern, pattern4, amap, bmap, stoc_len, lp, G, vcap,
+                        min(ra.shape[0], rb.shape[0]))
 
 
 # The default config (config=None) of each (D, sc_prec), built once with its
@@ -302,6 +306,7 @@ def _launch(gran: int, mode: str, a: torch.Tensor, b: torch.Tensor, sc_prec: int
         group_a=group_a, group_b=group_b, batch=batch, n=n, m=m, d=d,
         a=a.data_ptr(), b=b.data_ptr(), smooth_scales=smooth.data_ptr() if smooth is not None else None,
         out=out.data_ptr(), ktab=tables.ktab.data_ptr(), pattern=tables.pattern.data_ptr(),
+        pattern4=tables.pattern4.data_ptr(),
         amap=amap.data_ptr(), bmap=bmap.data_ptr(), vcap=tables.vcap, lp=tables.lp,
         flags=flags | (_lib.FLAG_FORCE_SIMT if _FORCE_SIMT else 0),
         tensor_ranges=ranges.data_ptr() if ranges is not None else None)

@@ -23,7 +23,7 @@ def declared_functions():
 def test_library_builds_and_loads():
     from scmp_kernels_b200 import build
     build.build()
-    assert _lib.load().scmp_abi_version() == _lib.ABI_VERSION == 2
+    assert _lib.load().scmp_abi_version() == _lib.ABI_VERSION == 3
 
 
 def test_every_declared_symbol_is_exported():
@@ -58,6 +58,6 @@ def test_invalid_arguments_are_rejected_without_gpu():
     assert lib.scmp_sc_matmul_workspace_size(ctypes.byref(d), ctypes.byref(size)) == _lib.SCMP_ERR_UNSUPPORTED
     with pytest.raises(NotImplementedError):
         _lib.check(_lib.SCMP_ERR_UNSUPPORTED)
-    assert lib.scmp_build_tables(None, 1, None, 1, 0, 32, 8, None, None, None) == _lib.SCMP_ERR_INVALID_ARG
+    assert lib.scmp_build_tables(None, 1, None, 1, 0, 32, 8, None, None, None, None) == _lib.SCMP_ERR_INVALID_ARG
     with pytest.raises(ValueError):
         _lib.check(_lib.SCMP_ERR_INVALID_ARG)

@@ -28,13 +28,16 @@ from scmp_kernels_b200.sc import kernels as K  # noqa: E402
 DEV = "cuda:0"
 
 
-@pytest.fixture(params=["tc2", "tc2atmem", "tc1", "simt"])
+@pytest.fixture(params=["tc2", "tc2int8", "tc2atmem", "tc1", "simt"])
 def impl(request, monkeypatch):
-    """tc2: tcgen05 on SM pairs (default: 512-wide tiles for long tiles, two
-    accumulators for short ones); tc2atmem: SM pairs with a in tensor memory
-    for long tiles; tc1: tcgen05 on single SMs; simt: CUDA cores."""
+    """tc2: tcgen05 on SM pairs (default: e2m1 operands for streams of 64
+    positions or more, 480-wide tiles for long tiles, two accumulators for
+    short ones); tc2int8: the same with int8 operands (512-wide tiles);
+    tc2atmem: SM pairs with a in tensor memory for long tiles; tc1: tcgen05
+    on single SMs; simt: CUDA cores."""
     monkeypatch.setattr(K, "_FORCE_SIMT", request.param == "simt")
     monkeypatch.setenv("SCMP_TC_ATMEM", "1" if request.param == "tc2atmem" else "0")
+    monkeypatch.setenv("SCMP_TC_INT8", "1" if request.param == "tc2int8" else "0")
     if request.param == "tc1":
         monkeypatch.setenv("SCMP_TC_SINGLE", "1")
     else:
@@ -86,6 +89,12 @@ def test_device_tables_reproduce_reference(L, G, env_vars):
     perm = 8 * (l & 3) + 4 * (l >> 4) + ((l >> 2) & 3)
     idx = (np.arange(sliced.shape[-1]) // 32) * 32 + perm[np.arange(sliced.shape[-1]) % 32]
     bits = sliced[..., idx]                                               # position order
+    # e2m1-sliced copy: word bit 4i + q holds position 8q + i of the word
+    pat4 = t.pattern4.cpu().numpy().view(np.uint32)[t.bmap.cpu().numpy()]
+    s4 = np.unpackbits(pat4.view(np.uint8), axis=-1, bitorder="little")
+    perm4 = 4 * (l & 7) + (l >> 3)
+    idx4 = (np.arange(s4.shape[-1]) // 32) * 32 + perm4[np.arange(s4.shape[-1]) % 32]
+    assert np.array_equal(s4[..., idx4], bits)
     cum = np.concatenate([np.zeros(bits.shape[:2] + (1,), np.int64), np.cumsum(bits, -1)], -1)
     ref = RNG[f"cum_L{L}_G{G}"]                                           # (6, L+1, V)
     vv = min(ref.shape[2], t.vcap + 1)
@@ -139,11 +148,14 @@ def test_tc_variants_match_simt_at_size(shape, kw, monkeypatch, env_vars):
     a = torch.randn(n, d, device=DEV, generator=g)
     b = torch.randn(m, d, device=DEV, generator=g) * 0.02
     outs = []
-    # CUDA cores; SM pairs (default); SM pairs with a in tensor memory; single SMs
-    for simt, single, atmem in ((True, "0", "0"), (False, "0", "0"), (False, "0", "1"), (False, "1", "0")):
+    # CUDA cores; SM pairs (default, e2m1); SM pairs with int8 operands; SM
+    # pairs with a in tensor memory; single SMs
+    for simt, single, atmem, i8 in ((True, "0", "0", "0"), (False, "0", "0", "0"), (False, "0", "0", "1"),
+                                    (False, "0", "1", "0"), (False, "1", "0", "0")):
         monkeypatch.setattr(K, "_FORCE_SIMT", simt)
         monkeypatch.setenv("SCMP_TC_SINGLE", single)
         monkeypatch.setenv("SCMP_TC_ATMEM", atmem)
+        monkeypatch.setenv("SCMP_TC_INT8", i8)
         outs.append(sc_matmul(a, b, **kw))
     for i, o in enumerate(outs[1:], 1):
         assert torch.equal(outs[0], o), f"variant {i} differs from the CUDA-core GEMM"
@@ -157,8 +169,8 @@ def test_tc_variants_match_simt_at_size(shape, kw, monkeypatch, env_vars):
     ((9, 197, 197, 640), dict(granularity="per_head", sc_prec=8)),                 # 9 heads, one tile each
     ((300, 700, 40), dict(granularity="per_row", sc_prec=8)),                    # 5 blocks: no tail
 ])
-@pytest.mark.parametrize("single", ["0", "1"])
-def test_split_last_wave_matches_whole_tiles(shape, kw, single, monkeypatch, env_vars):
+@pytest.mark.parametrize("single,i8", [("0", "0"), ("0", "1"), ("1", "0")])
+def test_split_last_wave_matches_whole_tiles(shape, kw, single, i8, monkeypatch, env_vars):
     """The last wave's tiles shared over K by all workers (pieces of uneven
     length, a worker's range spanning two tiles, the pieces' accumulators
     summed by the last to finish) give the same bits as whole tiles."""
@@ -174,6 +186,7 @@ def test_split_last_wave_matches_whole_tiles(shape, kw, single, monkeypatch, env
         b = torch.randn(m, d, device=DEV, generator=g) * 0.05
     monkeypatch.setattr(K, "_FORCE_SIMT", False)
     monkeypatch.setenv("SCMP_TC_SINGLE", single)
+    monkeypatch.setenv("SCMP_TC_INT8", i8)
     monkeypatch.setenv("SCMP_TC_NO_SPLIT", "0")
     y_split = sc_matmul(a, b, **kw)
     monkeypatch.setenv("SCMP_TC_NO_SPLIT", "1")
@@ -249,9 +262,10 @@ def test_native_kernels_do_the_work():
 def test_full_size_workloads_agree_across_gemm_variants(workload, rows, monkeypatch, env_vars):
     """The benchmark workloads at their full sizes (config 5: its first 512
     rows of a against all of b; per_row quantisation is row-local, so a row
-    slice is an exact sub-problem): the default GEMM (SM pairs, 512-wide
-    tiles, split last wave), SM pairs with a in tensor memory, and the
-    CUDA-core GEMM give the same bits, and every output is finite."""
+    slice is an exact sub-problem): the default GEMM (SM pairs, 480-wide
+    tiles, stream-K tail, e2m1 operands), the same with int8 operands, SM
+    pairs with a in tensor memory, and the CUDA-core GEMM give the same bits,
+    and every output is finite."""
     env_vars({})
     from scmp_kernels_b200 import workloads as W
     if workload == "config2":
@@ -266,9 +280,10 @@ def test_full_size_workloads_agree_across_gemm_variants(workload, rows, monkeypa
         a, b = (q, k) if workload == "config3qk" else (probs, v_t)
         kw = dict(granularity="per_head", sc_prec=8)
     outs = []
-    for simt, atmem in ((False, "0"), (False, "1"), (True, "0")):
+    for simt, atmem, i8 in ((False, "0", "0"), (False, "0", "1"), (False, "1", "0"), (True, "0", "0")):
         monkeypatch.setattr(K, "_FORCE_SIMT", simt)
         monkeypatch.setenv("SCMP_TC_ATMEM", atmem)
+        monkeypatch.setenv("SCMP_TC_INT8", i8)
         outs.append(sc_matmul(a, b, **kw))
     assert torch.isfinite(outs[0]).all()
     for i, o in enumerate(outs[1:], 1):

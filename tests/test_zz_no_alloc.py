@@ -37,7 +37,7 @@ def _desc(a, b, out, gran, mode, sc_prec, tables):
         stoc_len=tables.L, rng_levels=tables.G, chunk_d=0, group_a=1, group_b=1, batch=1, n=n,
         m=m, d=d, a=a.data_ptr(), b=b.data_ptr(), smooth_scales=None, out=out.data_ptr(),
         ktab=tables.ktab.data_ptr(), pattern=tables.pattern.data_ptr(), amap=amap.data_ptr(),
-        bmap=bmap.data_ptr(), vcap=tables.vcap, lp=tables.lp, flags=0)
+        bmap=bmap.data_ptr(), vcap=tables.vcap, lp=tables.lp, flags=0, pattern4=tables.pattern4.data_ptr())
     return desc, (amap, bmap)
 
 
