@@ -39,11 +39,11 @@ WORKLOADS = {
 
 
 # DRAM bytes of one GEMM launch (DRAM read + write bytes) from an ncu capture of
-# the 2048-row case of the config-2 recipe (370.6 MB,
-# profiles/gemm_tc_pair_wide512_2048x11008x4096.md), scaled to the 4096 rows of
-# the full workload: the a rows, the output and the bands of a that re-read b
-# all double.
-GEMM_TRAFFIC_BYTES = {"config2": 2 * 370.6e6}
+# the 2048-row case of the config-2 recipe (393.6 MB,
+# profiles/gemm_tc_pair_e2m1_wide480_2048x11008x4096.md), scaled to the 4096
+# rows of the full workload: the a rows, the output and the bands of a that
+# re-read b all double.
+GEMM_TRAFFIC_BYTES = {"config2": 2 * 393.6e6}
 
 
 def parse():
@@ -355,15 +355,25 @@ def main():
         except OSError:
             src = "fallback"
         bf16 = peaks.get("bf16_tflops", 1590.0)
-        int8_peak = 2.0 * bf16  # dense int8 tensor rate is twice the bf16 rate on B200
-        # the SC-GEMM is an int8 GEMM over K = D*L (sign x thermometer, sign x stream)
+        # The SC-GEMM is a GEMM over K = D*L with operands in {-1, 0, 1} (sign x
+        # thermometer, sign x stream). SM pairs run it on e2m1 operands
+        # (kind::mxf4, dense rate 4x bf16) for streams of 64 positions or more,
+        # else on int8 operands (kind::i8, dense rate 2x bf16).
+        env = os.environ
+        e2m1 = (env.get("SCMP_TC_INT8") != "1" and env.get("SCMP_TC_ATMEM") != "1"
+                and env.get("SCMP_TC_SINGLE") != "1" and (L is None or L > 32))
+        tc_peak = (4.0 if e2m1 else 2.0) * bf16
+        tc_unit = "TOPS (e2m1)" if e2m1 else "TOPS (int8)"
+        tc_src = (f"4 x bf16_tflops of {src} peaks (dense e2m1 = 4 x dense bf16)" if e2m1 else
+                  f"2 x bf16_tflops of {src} peaks (dense int8 = 2 x dense bf16)")
         Lw = L if L is not None else 149.33
         tensor_ops = 2.0 * BH * N * (M // world if world > 1 else M) * D * Lw
         achieved = tensor_ops / (gemm_ms * 1e-3) / 1e12
         line = {
             "metric": "SC-GEMM equiv GOPS (2*BH*N*M*D/s)", "value": value, "unit": "GOPS",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8xint8->int32",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "e2m1xe2m1->f32 (exact integer sums)" if e2m1 else "int8xint8->int32",
             "data": "synthetic (seeded, reference shapes and distributions)",
             "config": {"workload": args.workload, "desc": WORKLOADS[args.workload],
                        "l2": "inputs larger than L2 (b is 180 MB fp32)" if args.workload == "config2" else
@@ -372,11 +382,11 @@ def main():
                        else "single GPU"},
             "gpu_launches": launches,
             "gemm_ms_per_step": gemm_ms,
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS (int8)",
-                         "frac": achieved / int8_peak,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": tc_unit,
+                         "frac": achieved / tc_peak,
                          "traffic": (GEMM_TRAFFIC_BYTES.get(args.workload) if shape is None and world == 1
                                      else None),
-                         "peak_source": f"2 x bf16_tflops of {src} peaks (int8 dense = 2 x bf16 dense)"},
+                         "peak_source": tc_src},
             "clocks": clocks,
             "e2e": e2e,
         }

@@ -81,14 +81,18 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar)
                : "memory");
 }
+// The waiting thread may be suspended until the phase completes or
+// kSuspendHintNs nanoseconds pass, so that waiting warps do not take issue
+// slots from the working ones.
+constexpr uint32_t kSuspendHintNs = 1000000;
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "n"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }

@@ -2,28 +2,34 @@
 //
 // The reference's integer accumulator (sc/kernels.py:216-245)
 //   S[i][j] = sum_d sa*sb * #{t < k[i][d] : rb_d[t] < v[j][d]}
-// is an int8 GEMM over K = D * L:
+// is a GEMM over K = D * L:
 //   A'[i][(d,t)] = sa[i][d] * [t < k[i][d]]          (thermometer of a)
 //   B'[j][(d,t)] = sb[j][d] * [rb_d[t] < v[j][d]]    (comparator stream of b)
 // with every entry in {-1, 0, 1}. Neither operand exists in memory: producer
 // warps expand them per pipeline stage straight into shared memory, in the
 // canonical K-major 128-byte-swizzled layout, from the int16 operands of the
 // quantiser (signed k, signed v) and the bit-packed streams of the table
-// builder. One thread issues tcgen05.mma.kind::i8 (M=128, N=256, K=32) into
-// an int32 accumulator in tensor memory; epilogue warps read it back with
-// tcgen05.ld and apply the path's float32 recipe. The accumulation is exact.
+// builder. One thread issues the MMAs into an accumulator in tensor memory;
+// epilogue warps read it back with tcgen05.ld and apply the path's float32
+// recipe. The accumulation is exact.
+//
+// Operand types: e2m1 (4-bit floats 0, +1, -1; tcgen05.mma.kind::mxf4 with
+// every block scale 1.0, float32 accumulator holding integers below 2^24)
+// on SM pairs for streams of 64 to 512 positions, the default; int8
+// (kind::i8, int32 accumulator) otherwise. e2m1 halves the shared-memory
+// bytes and the producer work per K position and runs at twice the int8 MMA
+// rate.
 //
 // Two variants share this code (template parameter PAIR):
 //  - 1 SM per tile (cta_group::1): 128 a rows x 256 b rows per CTA; warps 0-3
 //    expand A' (one a row per thread), warps 4-11 expand B', warp 12 issues
 //    the MMAs, warps 13-16 run the epilogue;
-//  - 2 SMs per tile (cta_group::2, a cluster of two CTAs): 256 a rows x 256 b
-//    rows per pair; each CTA expands its 128 a rows and its half (128 rows)
-//    of B', so a stage moves 64 KB per SM through shared memory instead of
-//    96 KB. The leader CTA (rank 0) issues M=256 MMAs that read both CTAs'
-//    shared memory; producers of both CTAs signal the leader's "full"
-//    barriers, the leader's commits are multicast to both CTAs, and each CTA's
-//    epilogue reads its own 128 rows of the accumulator.
+//  - 2 SMs per tile (cta_group::2, a cluster of two CTAs): 256 a rows per
+//    pair; each CTA expands its 128 a rows and its half of B'. The leader CTA
+//    (rank 0) issues M=256 MMAs that read both CTAs' shared memory; producers
+//    of both CTAs signal the leader's "full" barriers, the leader's commits
+//    are multicast to both CTAs, and each CTA's epilogue reads its own 128
+//    rows of the accumulator.
 // Persistent grid over output tiles. Every mbarrier wait is bounded
 // (common.cuh): on timeout the kernel records SCMP_ERR_TIMEOUT, all roles
 // leave their loops, outstanding MMAs are drained and tensor memory is freed
