@@ -276,6 +276,17 @@ def output_to(peers, offset: int, ld: int, result: torch.Tensor):
         _REDIRECT.value = prev
 
 
+def _to_host(y: torch.Tensor) -> torch.Tensor:
+    """The result for host operands: copied into page-locked host memory (the
+    caching host allocator reuses it across calls), which transfers at the
+    full link rate, unlike a fresh pageable tensor that is faulted in page by
+    page during a synchronous copy."""
+    out = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+    out.copy_(y, non_blocking=True)
+    torch.cuda.current_stream(y.device).synchronize()
+    return out
+
+
 def _to_device(x: torch.Tensor) -> torch.Tensor:
     if x.device.type != "cuda":
         _lib.require_cuda()
@@ -376,7 +387,7 @@ def _sc_matmul_per_tensor(a, b, max_fp_a=None, min_fp_a=None, max_fp_b=None, min
         ranges = torch.tensor([float(max_fp_a), float(min_fp_a), float(mb), float(nb)],
                               dtype=torch.float64).to(a.device, non_blocking=True)
     y = _launch(_lib.PER_TENSOR, mode, a, b, sc_prec, t, smooth=s, flags=flags, ranges=ranges)
-    return y if dev_in.type == "cuda" else y.to(dev_in)
+    return y if dev_in.type == "cuda" else _to_host(y)
 
 
 @torch.no_grad()
@@ -394,7 +405,7 @@ def _sc_matmul_per_row(a, b, group_a=1, group_b=1, mode="unipolar", sc_prec=8, c
     t = _get_cached_enable_tables(config, sc_prec, a.device, stoc_len, rng_levels)
     y = _launch(_lib.PER_ROW, mode, a, b, sc_prec, t, group_a=group_a, group_b=group_b, smooth=s,
                 flags=flags)
-    return y if dev_in.type == "cuda" else y.to(dev_in)
+    return y if dev_in.type == "cuda" else _to_host(y)
 
 
 @torch.no_grad()
@@ -418,7 +429,7 @@ def _sc_matmul_per_row_mlp(a, b, mode="bipolar", sc_prec=8, config=None, group_a
     t = _get_cached_enable_tables(config, sc_prec, a.device, stoc_len, rng_levels)
     y = _launch(_lib.PER_ROW, mode, a, b, sc_prec, t, chunk_d=chunk_d, smooth=s, period=chunk_d,
                 flags=flags)
-    return y if dev_in.type == "cuda" else y.to(dev_in)
+    return y if dev_in.type == "cuda" else _to_host(y)
 
 
 @torch.no_grad()
@@ -444,7 +455,7 @@ def _sc_matmul_per_row_batched(a, b, group_a=1, group_b=1, mode="bipolar", sc_pr
     t = _get_cached_enable_tables(config, sc_prec, a.device, stoc_len, rng_levels)
     y = _launch(_lib.PER_ROW, mode, a, b, sc_prec, t, group_a=group_a, group_b=group_b, smooth=s,
                 flags=flags)
-    return y if dev_in.type == "cuda" else y.to(dev_in)
+    return y if dev_in.type == "cuda" else _to_host(y)
 
 
 @torch.no_grad()
@@ -467,7 +478,7 @@ def _sc_matmul_per_head_bipolar(q_flat, k_flat, sc_prec=8, config=None, stoc_len
     config = _default_config(config, D, sc_prec)
     t = _get_cached_enable_tables(config, sc_prec, a.device, stoc_len, rng_levels)
     y = _launch(_lib.PER_HEAD, "bipolar", a, b, sc_prec, t, smooth=s, flags=flags)
-    return y if dev_in.type == "cuda" else y.to(dev_in)
+    return y if dev_in.type == "cuda" else _to_host(y)
 
 
 # Re-exports kept for callers that import the quantisers from this module
