@@ -144,15 +144,18 @@ def _sc_matmul_impl(
     return _sc_matmul_per_head_bipolar(a, b, **kw)
 
 
-# Host operands: the rows of a are processed in KA blocks. The first block runs
-# against b's row blocks as they arrive (b is copied to the device block by
-# block on a copy stream while the previous block computes); the later blocks
-# run against the whole of b. Each finished block of result rows (contiguous
-# in memory) is copied back on a second copy stream while the next block
-# computes. Applies to 2D per_row calls with both operands in pinned host
-# memory and a CUDA device present; per_row quantisation is row-local (row
-# groups are kept whole), so the blocks give the same bits as one call.
-_HOST_A_BLOCKS = 4        # blocks of a's rows
+# Host operands: the rows of a are processed in three blocks, a quarter, a
+# half and a quarter of the rows. The first block runs against b's row blocks
+# as they arrive (b is copied to the device block by block on a copy stream
+# while the previous block computes); the later blocks run against the whole
+# of b (the middle one is one call, so that fewer, larger GEMMs run; the last
+# one is a quarter, so that little result is left to copy back after the last
+# GEMM). Each finished block of result rows (contiguous in memory) is copied
+# back on a second copy stream while the next block computes. Applies to 2D
+# per_row calls with both operands in pinned host memory and a CUDA device
+# present; per_row quantisation is row-local (row groups are kept whole), so
+# the blocks give the same bits as one call.
+_HOST_A_FIRST = 4         # the first block is 1/_HOST_A_FIRST of a's rows, and so is the last
 _HOST_B_BLOCKS = 4        # blocks of b's rows in the first pass
 _HOST_MIN_ROWS = 1024     # smaller calls are not split
 
@@ -172,7 +175,8 @@ def _per_row_host_pipelined(a: torch.Tensor, b: torch.Tensor, run, group_a: int,
     from . import kernels as K
     dev = torch.device("cuda", torch.cuda.current_device())
     n, m = a.shape[0], b.shape[0]
-    a_blocks = _blocks(n, (n + _HOST_A_BLOCKS - 1) // _HOST_A_BLOCKS, group_a)
+    q = _blocks(n, (n + _HOST_A_FIRST - 1) // _HOST_A_FIRST, group_a)  # quarters
+    a_blocks = [q[0], (q[1][0], q[-2][1]), q[-1]] if len(q) > 3 else q
     b_blocks = _blocks(m, (m + _HOST_B_BLOCKS - 1) // _HOST_B_BLOCKS, group_b)
     comp = torch.cuda.current_stream(dev)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
