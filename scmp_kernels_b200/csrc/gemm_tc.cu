@@ -474,7 +474,7 @@ __device__ __forceinline__ int stages_of_unit(int len) {
 // memory at tmem_a (this thread's lane, first stage column) instead.
 // With F4 the words are e2m1: eight 4-bit values (0, +1 = 0x2, -1 = 0xA) per
 // 32-bit word, so a 16-byte chunk covers 32 positions instead of 16.
-template <bool SIDE_A, int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE, bool F4>
+template <bool SIDE_A, int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE, bool F4, bool UNR>
 __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint32_t sbase, uint32_t bar_base,
                                         volatile int* abort_flag, uint32_t rank, int tile0, int tstep, int r,
                                         int lane, uint32_t tmem_a) {
@@ -541,8 +541,16 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
           }
         }
         const int jmax = min(NSPB, nst - blk * NSPB);
-#pragma unroll 1
-        for (int j = 0; j < jmax; ++j) {
+        // UNR (e2m1 long tiles and the chunked path): the block's stages are
+        // unrolled, so every dimension index below is a compile-time constant
+        // (no selects on kv, bm); measured 6.7% faster on config 2 and 4.5%
+        // on config 4. int8 (twice the stages per block) keeps the loop
+        // rolled so that it stays in the instruction cache, and so do the
+        // short-tile kernels (slower unrolled).
+        constexpr int UNROLL = UNR ? NSPB : 1;
+#pragma unroll UNROLL
+        for (int j = 0; j < NSPB; ++j) {
+          if (j >= jmax) break;
           uint32_t pn[NPW];
           if (!SIDE_A) {
             if (j + 1 < NSPB)
@@ -661,7 +669,7 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
 
 // TLEN: padded stream length lp when lp <= 256 (256/lp dimensions per stage),
 // or 256 when lp = 256*SPD (SPD stages per dimension, SPD = 1 or 2).
-template <int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE, bool F4>
+template <int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE, bool F4, bool UNR>
 __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched sc) {
   using C = Cfg<PAIR, ATMEM, WIDE, F4>;
   constexpr int NST = C::NST;
@@ -800,10 +808,10 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
     // ------------------------------------------------------------ producers
     // a's warp w writes tensor-memory lanes 32w..32w+31 (its rows)
     if (warp < PROD_A_WARPS)
-      produce<true, TLEN, SPD, PAIR, ATMEM, WIDE, F4>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep, threadIdx.x,
+      produce<true, TLEN, SPD, PAIR, ATMEM, WIDE, F4, UNR>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep, threadIdx.x,
                                             lane, tmem + ((uint32_t)(32 * warp) << 16) + C::TMEM_A);
     else
-      produce<false, TLEN, SPD, PAIR, ATMEM, WIDE, F4>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep,
+      produce<false, TLEN, SPD, PAIR, ATMEM, WIDE, F4, UNR>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep,
                                              threadIdx.x - PROD_A_WARPS * 32, lane, 0u);
   } else if (!C::MERGED && warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer (leader CTA)
@@ -1019,11 +1027,12 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
   }
 }
 
-template <int TLEN, int SPD, bool PAIR, bool ATMEM = false, bool WIDE = ATMEM && wide_tiles<TLEN>(), bool F4 = false>
+template <int TLEN, int SPD, bool PAIR, bool ATMEM = false, bool WIDE = ATMEM && wide_tiles<TLEN>(), bool F4 = false,
+          bool UNR = F4 && WIDE>
 static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int sms, cudaStream_t st) {
   using C = Cfg<PAIR, ATMEM, WIDE, F4>;
   static bool attr = false;
-  auto kern = gemm_tc_kernel<TLEN, SPD, PAIR, ATMEM, WIDE, F4>;
+  auto kern = gemm_tc_kernel<TLEN, SPD, PAIR, ATMEM, WIDE, F4, UNR>;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
@@ -1211,6 +1220,14 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
         case 128: return launch_t<128, 1, true, false, true, true>(g, s, sms, st);
         case 256: return launch_t<256, 1, true, false, true, true>(g, s, sms, st);
         default: return launch_t<512, 1, true, false, true, true>(g, s, sms, st);
+      }
+    }
+    if (s.nunits > 1) {  // chunked path: stages unrolled
+      switch (g.lp) {
+        case 64: return launch_t<64, 1, true, false, false, true, true>(g, s, sms, st);
+        case 128: return launch_t<128, 1, true, false, false, true, true>(g, s, sms, st);
+        case 256: return launch_t<256, 1, true, false, false, true, true>(g, s, sms, st);
+        default: return launch_t<512, 1, true, false, false, true, true>(g, s, sms, st);
       }
     }
     switch (g.lp) {
