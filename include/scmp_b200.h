@@ -47,6 +47,17 @@ enum scmp_mode { SCMP_BIPOLAR = 0, SCMP_UNIPOLAR = 1 };
 #define SCMP_FLAG_FORCE_SIMT 0x1 /* use the CUDA-core GEMM instead of tcgen05  */
 #define SCMP_FLAG_NO_SPLIT 0x2   /* do not split the last wave of output tiles
                                     over K (smaller workspace, longer tail)     */
+/* SCMP_FLAG_B_READY: per_row calls without chunking only. b's quantised
+ * operand and row parameters are already in the workspace, left there by an
+ * earlier scmp_sc_matmul call on the same workspace with the same b and the
+ * same b-side arguments (m, d, batch, mode, sc_prec, stoc_len, rng_levels,
+ * group_b, smooth_scales, tables); b's quantisation is skipped and `b` is not
+ * read (it may be NULL). b's part of the workspace sits at its start and does
+ * not depend on n, so one workspace serves calls with any a that fits it: a
+ * static weight is quantised once (no counterpart in the reference, which
+ * quantises both operands on every call; its SmoothQuant offline helper,
+ * quant/smoothquant.py:129-147, is the analogue for the smoothing step). */
+#define SCMP_FLAG_B_READY 0x4
 
 /*
  * Enable-signal tables (the "RNG cache" kept resident in HBM).

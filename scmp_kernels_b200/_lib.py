@@ -26,6 +26,7 @@ PER_TENSOR, PER_ROW, PER_HEAD = 0, 1, 2
 BIPOLAR, UNIPOLAR = 0, 1
 FLAG_FORCE_SIMT = 0x1
 FLAG_NO_SPLIT = 0x2
+FLAG_B_READY = 0x4
 ABI_VERSION = 3
 MAX_OUT_PEERS = 8
 

@@ -77,6 +77,11 @@ struct Plan {
   int* split_cnt = nullptr;
 };
 
+static bool is_chunked(const scmp_matmul_desc* d) {
+  return d->granularity == SCMP_PER_ROW && d->chunk_d > 0 && d->mode == SCMP_BIPOLAR &&
+         d->batch == 1 && d->d > d->chunk_d;
+}
+
 static int validate(const scmp_matmul_desc* d) {
   if (!d) return fail(SCMP_ERR_INVALID_ARG, "sc_matmul: null descriptor");
   if (d->granularity < SCMP_PER_TENSOR || d->granularity > SCMP_PER_HEAD)
@@ -85,6 +90,8 @@ static int validate(const scmp_matmul_desc* d) {
     return fail(SCMP_ERR_INVALID_ARG, "sc_matmul: unknown mode");
   if (d->granularity == SCMP_PER_HEAD && d->mode != SCMP_BIPOLAR)
     return fail(SCMP_ERR_INVALID_ARG, "sc_matmul: granularity='per_head' currently only supports mode='bipolar'");
+  if ((d->flags & SCMP_FLAG_B_READY) && (d->granularity != SCMP_PER_ROW || is_chunked(d)))
+    return fail(SCMP_ERR_INVALID_ARG, "sc_matmul: SCMP_FLAG_B_READY applies to per_row calls without chunk_d");
   const int pmin = d->mode == SCMP_BIPOLAR ? 2 : 1;
   if (d->sc_prec < pmin || d->sc_prec > 15)
     return fail(SCMP_ERR_INVALID_ARG, "sc_matmul: sc_prec out of range (bipolar 2..15, unipolar 1..15)");
@@ -111,28 +118,25 @@ static int validate(const scmp_matmul_desc* d) {
   return SCMP_OK;
 }
 
-static bool is_chunked(const scmp_matmul_desc* d) {
-  return d->granularity == SCMP_PER_ROW && d->chunk_d > 0 && d->mode == SCMP_BIPOLAR &&
-         d->batch == 1 && d->d > d->chunk_d;
-}
 
 static void carve(const scmp_matmul_desc* d, Carver& c, Plan& p) {
   const size_t na = (size_t)d->batch * d->n, nb = (size_t)d->batch * d->m;
   const size_t dd = (size_t)d8(d->d) * 8;
-  p.ka = c.take<int16_t>(na * dd);
-  p.vb = c.take<int16_t>(nb * dd);
-  p.bmap = c.take<int32_t>(dd);
   p.chunked = is_chunked(d);
   p.nchunks = p.chunked ? cdiv(d->d, d->chunk_d) : 1;
   const size_t rows_a = p.chunked ? na * p.nchunks : na, rows_b = p.chunked ? nb * p.nchunks : nb;
-  p.stats_a = c.take<float>(3 * na);
+  // b's buffers first: their offsets do not depend on n (SCMP_FLAG_B_READY)
+  p.vb = c.take<int16_t>(nb * dd);
   p.stats_b = c.take<float>(3 * nb);
-  p.scale_a = c.take<float>(rows_a > (size_t)d->batch ? rows_a : d->batch);
   p.scale_b = c.take<float>(rows_b > (size_t)d->batch ? rows_b : d->batch);
-  p.zp_a = c.take<float>(na > (size_t)d->batch ? na : d->batch);
   p.zp_b = c.take<float>(nb > (size_t)d->batch ? nb : d->batch);
-  p.sum_a = c.take<float>(na);
   p.sum_b = c.take<float>(nb);
+  p.ka = c.take<int16_t>(na * dd);
+  p.bmap = c.take<int32_t>(dd);
+  p.stats_a = c.take<float>(3 * na);
+  p.scale_a = c.take<float>(rows_a > (size_t)d->batch ? rows_a : d->batch);
+  p.zp_a = c.take<float>(na > (size_t)d->batch ? na : d->batch);
+  p.sum_a = c.take<float>(na);
   p.scal = c.take<float>(8);
   if (!(d->flags & (SCMP_FLAG_FORCE_SIMT | SCMP_FLAG_NO_SPLIT))) {
     const int unit_d = p.chunked ? d->chunk_d : d->d;
@@ -262,7 +266,9 @@ int scmp_sc_matmul(const scmp_matmul_desc* d, void* workspace, size_t workspace_
   int s = validate(d);
   if (s) return s;
   if (d->n == 0 || d->m == 0) return SCMP_OK;
-  if (!d->a || !d->b || (!d->out && d->n_out_peers == 0) || !d->ktab || !d->pattern || !d->amap || !d->bmap)
+  const bool b_ready = (d->flags & SCMP_FLAG_B_READY) != 0;
+  if (!d->a || (!d->b && !b_ready) || (!d->out && d->n_out_peers == 0) || !d->ktab || !d->pattern || !d->amap ||
+      !d->bmap)
     return fail(SCMP_ERR_INVALID_ARG, "sc_matmul: null operand, output or table pointer");
   for (int k = 0; k < d->n_out_peers; ++k)
     if (!d->out_peers[k]) return fail(SCMP_ERR_INVALID_ARG, "sc_matmul: null out_peers entry");
@@ -376,6 +382,7 @@ int scmp_sc_matmul(const scmp_matmul_desc* d, void* workspace, size_t workspace_
     float* zps[2] = {p.zp_a, p.zp_b};
     float* sums[2] = {p.sum_a, p.sum_b};
     for (int i = 0; i < 2; ++i) {
+      if (i == 1 && b_ready) break;  // b's operand, scales, zero points, sums: in the workspace
       QuantArgs& o = *ops[i];
       o.row_scale = scales[i];
       o.row_zp = zps[i];

@@ -52,6 +52,8 @@ extern "C" int scmp_sc_matmul_noalloc(const scmp_matmul_desc* desc, void* stream
   size_t need = 0;
   int s = scmp_sc_matmul_workspace_size(desc, &need);
   if (s) return s;
+  if (desc->flags & SCMP_FLAG_B_READY)  // the shared array keeps no weight between calls
+    return fail(SCMP_ERR_INVALID_ARG, "sc_matmul_noalloc: SCMP_FLAG_B_READY needs a caller-owned workspace");
   scmp_matmul_desc whole;
   if (need > kNoAllocScratchBytes && !(desc->flags & SCMP_FLAG_NO_SPLIT)) {
     // without the split last wave's part accumulators the call may still fit

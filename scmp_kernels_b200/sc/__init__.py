@@ -9,5 +9,7 @@
 """
 from .kernels import clear_rng_cache, det_kernel_tuning
 from .matmul import sc_matmul
+from .prepared import PreparedWeight, prepare_weight, sc_matmul_prepared
 
-__all__ = ["sc_matmul", "clear_rng_cache", "det_kernel_tuning"]
+__all__ = ["sc_matmul", "clear_rng_cache", "det_kernel_tuning", "PreparedWeight", "prepare_weight",
+           "sc_matmul_prepared"]

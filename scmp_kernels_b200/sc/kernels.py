@@ -298,7 +298,8 @@ def _launch(gran: int, mode: str, a: torch.Tensor, b: torch.Tensor, sc_prec: int
             *, group_a=1, group_b=1, chunk_d=0, smooth: Optional[torch.Tensor] = None,
             period: Optional[int] = None, out: Optional[torch.Tensor] = None,
             workspace: Optional[torch.Tensor] = None, flags: int = 0,
-            ranges: Optional[torch.Tensor] = None) -> torch.Tensor:
+            ranges: Optional[torch.Tensor] = None, b_ready: bool = False,
+            workspace_out: Optional[list] = None) -> torch.Tensor:
     """One ``scmp_sc_matmul`` call. a: (batch, n, d) or (n, d); b likewise."""
     three_d = a.dim() == 3
     batch = a.shape[0] if three_d else 1
@@ -330,6 +331,11 @@ def _launch(gran: int, mode: str, a: torch.Tensor, b: torch.Tensor, sc_prec: int
     _lib.check(L.scmp_sc_matmul_workspace_size(ctypes.byref(desc), ctypes.byref(ws_bytes)), "sc_matmul")
     if workspace is None or workspace.numel() < ws_bytes.value:
         workspace = torch.empty(max(ws_bytes.value, 1), dtype=torch.uint8, device=dev)
+        b_ready = False  # a new workspace holds no quantised b
+    if b_ready:  # b's quantised operand is in `workspace` from an earlier call
+        desc.flags |= _lib.FLAG_B_READY
+    if workspace_out is not None:
+        workspace_out.append(workspace)
     _lib.check(L.scmp_sc_matmul(ctypes.byref(desc), ctypes.c_void_p(workspace.data_ptr()),
                                 ws_bytes.value, ctypes.c_void_p(_lib.stream_handle(dev))), "sc_matmul")
     return out

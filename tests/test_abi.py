@@ -58,6 +58,16 @@ def test_invalid_arguments_are_rejected_without_gpu():
     assert lib.scmp_sc_matmul_workspace_size(ctypes.byref(d), ctypes.byref(size)) == _lib.SCMP_ERR_UNSUPPORTED
     with pytest.raises(NotImplementedError):
         _lib.check(_lib.SCMP_ERR_UNSUPPORTED)
+    # b already quantised in the workspace: per_row without chunking only
+    d.batch, d.group_a = 1, 1
+    d.flags = _lib.FLAG_B_READY
+    assert lib.scmp_sc_matmul_workspace_size(ctypes.byref(d), ctypes.byref(size)) == _lib.SCMP_OK
+    d.granularity = _lib.PER_TENSOR
+    assert lib.scmp_sc_matmul_workspace_size(ctypes.byref(d), ctypes.byref(size)) == _lib.SCMP_ERR_INVALID_ARG
+    assert b"B_READY" in lib.scmp_last_error()
+    d.granularity, d.chunk_d, d.d = _lib.PER_ROW, 4, 8
+    assert lib.scmp_sc_matmul_workspace_size(ctypes.byref(d), ctypes.byref(size)) == _lib.SCMP_ERR_INVALID_ARG
+    d.flags, d.chunk_d = 0, 0
     assert lib.scmp_build_tables(None, 1, None, 1, 0, 32, 8, None, None, None, None) == _lib.SCMP_ERR_INVALID_ARG
     with pytest.raises(ValueError):
         _lib.check(_lib.SCMP_ERR_INVALID_ARG)

@@ -91,3 +91,15 @@ def test_smoothing_invalid_args():
         compute_smooth_scales(torch.ones(8), torch.ones(4, 9))
     with pytest.raises(ValueError):
         apply_smoothing(torch.zeros(2, 8), torch.zeros(3, 8), torch.zeros(2, 8))
+
+
+def test_prepare_weight_argument_checks():
+    from scmp_kernels_b200 import prepare_weight
+    with pytest.raises(ValueError, match="mode"):
+        prepare_weight(torch.zeros(4, 8), mode="ternary")
+    with pytest.raises(ValueError, match="2D"):
+        prepare_weight(torch.zeros(2, 4, 8))
+    with pytest.raises(ValueError, match="float32"):
+        prepare_weight(torch.zeros(4, 8, dtype=torch.float16), smooth_scales=torch.ones(8))
+    with pytest.raises(ValueError, match="smooth_scales"):
+        prepare_weight(torch.zeros(4, 8), smooth_scales=torch.ones(7))

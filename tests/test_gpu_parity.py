@@ -332,3 +332,37 @@ def test_cpu_inputs_round_trip_and_device_guard():
     assert torch.cuda.current_device() == 0
     y2 = sc_matmul(a.cuda(), b.cuda(), "per_row")
     assert torch.equal(y, y2.cpu())
+
+
+@pytest.mark.parametrize("kw", [
+    dict(mode="bipolar", sc_prec=8),
+    dict(mode="unipolar", sc_prec=6, stoc_len=64, group_b=4),
+    dict(mode="bipolar", sc_prec=8, smooth=True),
+])
+def test_prepared_weight_matches_sc_matmul(kw, env_vars):
+    """A weight quantised once (prepare_weight / sc_matmul_prepared, the
+    library's SCMP_FLAG_B_READY) gives the bits of sc_matmul on every call: a
+    sequence of a's with growing and shrinking row counts (the workspace grows
+    once, b is quantised again then), and, once quantised, b is not read
+    (zeroing it leaves the results unchanged)."""
+    from scmp_kernels_b200 import prepare_weight, sc_matmul_prepared
+    env_vars({})
+    kw = dict(kw)
+    g = torch.Generator(device=DEV).manual_seed(21)
+    d, m = 640, 1100
+    b = torch.randn(m, d, device=DEV, generator=g) * 0.03
+    if kw.pop("smooth", False):
+        kw["smooth_scales"] = torch.rand(d, device=DEV, generator=g) + 0.5
+    w = prepare_weight(b, **kw)
+    refs = {}
+    for n in (300, 1500, 64, 1500):
+        a = torch.randn(n, d, device=DEV, generator=torch.Generator(device=DEV).manual_seed(n))
+        ref = sc_matmul(a, b, "per_row", **kw)
+        y = sc_matmul_prepared(a, w)
+        assert torch.equal(y, ref), f"n={n}"
+        refs[n] = (a, ref)
+    b.zero_()  # the prepared weight refers to b; the workspace already holds it quantised
+    for n in (300, 64):
+        a, ref = refs[n]
+        assert torch.equal(sc_matmul_prepared(a, w), ref)
+    assert _lib.device_error() == 0
