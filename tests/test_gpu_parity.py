@@ -227,7 +227,8 @@ def test_result_scattered_to_several_buffers(gran, shape, simt, monkeypatch, env
 
 
 @pytest.mark.parametrize("kw", [dict(sc_prec=8), dict(sc_prec=6, mode="unipolar", stoc_len=64, group_b=7),
-                                dict(sc_prec=8, chunk_d=64, stoc_len=128, rng_levels=128)])
+                                dict(sc_prec=8, chunk_d=64, stoc_len=128, rng_levels=128),
+                                dict(sc_prec=8, group_a=5), dict(sc_prec=6, mode="unipolar", stoc_len=32, group_a=3)])
 def test_host_operands_pipelined_equal_device_result(kw, env_vars):
     """Pinned host operands take the streamed path (b and the result moved in
     blocks while blocks compute); the result equals the device call's."""
