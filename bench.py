@@ -252,7 +252,11 @@ def main():
             y[idx] = yi
         return y
 
-    clk_p, clk_f = clocks_start(local)  # sampled from warm-up to the end of the timed steps
+    # rank 0's GPU is sampled from warm-up to the end of the timed steps (the
+    # line reports rank 0's clocks); the other GPUs are not polled, since an
+    # nvidia-smi query can briefly stall a GPU and the per-call barrier of the
+    # sharded path would pass every rank's stall on to all of them
+    clk_p, clk_f = clocks_start(local) if rank == 0 else (None, None)
     if clk_p is not None:
         clocks_wait_first_sample(clk_f)
     for _ in range(args.warmup):
