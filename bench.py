@@ -1,18 +1,31 @@
 """Benchmark of the B200 stochastic-computing matmul (one JSON line on rank 0).
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--workload config2|config5|config3qk|config3av|config4]
-                [--impl ours|reference]
+                [--side config5,...|none] [--impl ours|reference]
 
 Metric: equivalent SC-GEMM throughput, 2*BH*N*M*D / t, in GOPS (the
-reference's headline). A step is one sc_matmul over the workload's resident
-operands. At N > 1 the weight operand b is sharded by rows over the ranks and
-the output column blocks are all-gathered with NCCL (strong scaling: the job's
-total work is fixed). `value` is device-timed (CUDA events, max over ranks);
-`e2e` times the public API end to end from pinned host buffers (inputs copied
-host->device and the output read back every step). `--impl reference` times
-the CPU oracle port of the reference's algorithm on a bounded sample of the
-same workload with all host threads (the reference itself is Python + Triton
-and only runs on the CPU under its interpreter, which the oracle restates).
+reference's headline), with bit-ops/s = BH*N*M*D*L / t beside it. A step is
+one sc_matmul over the workload's resident operands. At N > 1 the weight
+operand b is sharded by rows over the ranks and each rank's column block is
+stored into every rank's full output by the GEMM's own epilogue (strong
+scaling: the job's total work is fixed). `value` is device-timed (CUDA
+events, max over ranks); `e2e` times the public API end to end from pinned
+host buffers (inputs copied host->device and the result read back every
+step; at N > 1 each rank copies in a and its shard of b and reads back its
+own column block). At N > 1 the line carries `check`: every rank compares
+the first and the last 128 rows of its gathered output with a single-GPU
+sc_matmul of those rows against the whole of b, bit for bit, and the run
+exits non-zero on a mismatch. `--side` adds the same measurement of other
+workloads as nested objects (default: config 5, the north_star's scaling
+shape, at every N).
+
+At N = 1 rank 0 also reports: `cpu_baseline`, the C/OpenMP restatement of
+the reference's algorithm on a bounded row slice with all host threads;
+`reference_gpu`, the reference's own Triton path run on this B200
+(baseline/reference_runs.py gpu) with its output compared bit for bit;
+`cpu_baseline_interpreter`, the reference's own CPU path (the Triton
+interpreter) on configuration 1. `--impl reference` times the C restatement
+as the reference arm.
 """
 from __future__ import annotations
 
@@ -22,14 +35,13 @@ import os
 import statistics
 import subprocess
 import sys
-import tempfile
+import threading
 import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 WORKLOADS = {
-    # name: (description, builder)
     "config2": "per_row bipolar, Llama-7B MLP up-proj: a 4096x4096, b 11008x4096, p=8, L=256",
     "config5": "per_row unipolar + SmoothQuant, Llama-70B MLP: a 8192x8192, b 28672x8192, p=6, L=64",
     "config3qk": "per_head bipolar ViT-B/16 QK: 768 x (197x64) x (197x64), p=8, L=256",
@@ -37,13 +49,17 @@ WORKLOADS = {
     "config4": "per_row bipolar chunk_d=64 ViT-B fc2: a 12608x3072, b 768x3072, p=8, L=256/128/64 by row-range tercile",
 }
 
-
 # DRAM bytes of one GEMM launch (DRAM read + write bytes) from an ncu capture of
-# the 2048-row case of the config-2 recipe (395.7 MB,
-# profiles/gemm_tc_pair_e2m1_wide480_2048x11008x4096.md), scaled to the 4096
-# rows of the full workload: the a rows, the output and the bands of a that
-# re-read b all double.
+# the 2048-row case of the config-2 recipe (395.7 MB), scaled to the 4096 rows
+# of the full workload: the a rows, the output and the bands of a that re-read
+# b all double.
 GEMM_TRAFFIC_BYTES = {"config2": 2 * 395.7e6}
+
+# Dense tensor-core multiply-accumulates per SM and clock on B200, by operand
+# type (bf16 4096, int8 8192, e2m1 16384), for the fraction of the nominal
+# rate at the sampled SM clock.
+MACS_PER_SM_CLK = {"e2m1": 16384, "int8": 8192}
+B200_SMS = 148
 
 
 def parse():
@@ -52,17 +68,20 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="config2", choices=sorted(WORKLOADS))
+    ap.add_argument("--side", default="config5",
+                    help="comma-separated extra workloads measured the same way, or 'none'")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-runs", action="store_true",
+                    help="skip the reference's GPU and interpreter runs at N=1")
     ap.add_argument("--shape", default=None,
                     help="N,M,D override of the config2/config5 recipes (smaller cases for profiling)")
     return ap.parse_args()
 
 
 def build_workload(name, device, shape=None):
-    """Returns (a, b, kwargs, bh_n_m_d, L, label, calls) with calls = list of
-    (a_rows_index or None, kwargs) for workloads composed of several calls."""
+    """(a, b, smooth_scales, kwargs, (BH, N, M, D), L) of a workload."""
     from scmp_kernels_b200 import workloads as W
     if name == "config2":
         n, m, d = shape or (4096, 11008, 4096)
@@ -85,65 +104,106 @@ def build_workload(name, device, shape=None):
     raise ValueError(name)
 
 
-def clocks_start(idx):
-    f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-    q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-    try:
-        p = subprocess.Popen(["nvidia-smi", f"--id={idx}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                              "-lms", "200"], stdout=f, stderr=subprocess.DEVNULL)
-    except OSError:
-        p = None
-    return p, f.name
+# ---------------------------------------------------------------------------
+# clocks: NVML read in-process (the fields of nvidia-smi's clocks query, read
+# only; a sampler subprocess polling the GPU was seen to stall it), with the
+# nvidia-smi subprocess as the fallback
+# ---------------------------------------------------------------------------
 
-
-def clocks_wait_first_sample(path, timeout_s=10.0):
-    """Block until the sampler has written its first line, so that its start-up
-    (NVML initialisation) happens before the timed region, not inside it."""
-    t0 = time.time()
-    while time.time() - t0 < timeout_s:
+class ClockSampler:
+    def __init__(self, cuda_index: int, period_s: float = 0.2):
+        self.period, self.samples, self.kind = period_s, [], None
+        self._stop, self._thread, self._proc, self._file = threading.Event(), None, None, None
         try:
-            if os.path.getsize(path) > 0:
-                return
+            import pynvml as P
+            import torch
+            P.nvmlInit()
+            try:
+                h = P.nvmlDeviceGetHandleByUUID("GPU-" + str(torch.cuda.get_device_properties(cuda_index).uuid))
+            except Exception:  # noqa: BLE001
+                h = P.nvmlDeviceGetHandleByIndex(cuda_index)
+            self.P, self.h, self.kind = P, h, "nvml"
+            self.max_mhz = float(P.nvmlDeviceGetMaxClockInfo(h, P.NVML_CLOCK_SM))
+            self.bits = {"hw_slowdown": P.nvmlClocksEventReasonHwSlowdown,
+                         "hw_thermal_slowdown": P.nvmlClocksEventReasonHwThermalSlowdown,
+                         "sw_thermal_slowdown": P.nvmlClocksEventReasonSwThermalSlowdown,
+                         "sw_power_cap": P.nvmlClocksEventReasonSwPowerCap}
+        except Exception:  # noqa: BLE001
+            self.kind = "nvidia-smi"
+            self.idx = cuda_index
+
+    def _loop(self):
+        P, h = self.P, self.h
+        while not self._stop.is_set():
+            try:
+                sm = float(P.nvmlDeviceGetClockInfo(h, P.NVML_CLOCK_SM))
+                rs = int(P.nvmlDeviceGetCurrentClocksEventReasons(h))
+                pw = P.nvmlDeviceGetPowerUsage(h) / 1000.0
+                self.samples.append((sm, self.max_mhz, pw, [n for n, b in self.bits.items() if rs & b]))
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(self.period)
+
+    def start(self):
+        self.samples = []
+        self._stop.clear()
+        if self.kind == "nvml":
+            self._thread = threading.Thread(target=self._loop, daemon=True)
+            self._thread.start()
+            return
+        import tempfile
+        self._file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False).name
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self._proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={q}",
+                                           "--format=csv,noheader,nounits", "-lms", "200"],
+                                          stdout=open(self._file, "w"), stderr=subprocess.DEVNULL)
         except OSError:
-            pass
-        time.sleep(0.05)
+            self._proc = None
+        t0 = time.time()  # let the sampler start before the timed region
+        while self._proc is not None and time.time() - t0 < 10 and os.path.getsize(self._file) == 0:
+            time.sleep(0.05)
+
+    def stop(self):
+        if self.kind == "nvml":
+            self._stop.set()
+            if self._thread is not None:
+                self._thread.join(timeout=5)
+        elif self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for line in open(self._file):
+                f = [x.strip() for x in line.split(",")]
+                try:
+                    self.samples.append((float(f[1]), float(f[2]), float(f[3]),
+                                         [n for n, v in zip(names, f[5:9]) if v.lower() == "active"]))
+                except (ValueError, IndexError):
+                    continue
+            os.unlink(self._file)
+        if not self.samples:
+            return None
+        mx = self.samples[-1][1]
+        sms = [s[0] for s in self.samples]
+        load = [s for s in sms if mx and s > 0.5 * mx] or sms
+        reasons = sorted({r for s in self.samples for r in s[3]})
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(sms), "power_w_max": max(s[2] for s in self.samples), "sampler": self.kind}
 
 
-def clocks_stop(p, path):
-    if p is None:
-        return None
-    p.terminate()
-    try:
-        p.wait(timeout=5)
-    except subprocess.TimeoutExpired:
-        p.kill()
-    sms, mx, reasons = [], None, set()
-    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-    for line in open(path):
-        f = [x.strip() for x in line.split(",")]
-        if len(f) < 9:
-            continue
-        try:
-            sms.append(float(f[1]))
-            mx = float(f[2])
-        except ValueError:
-            continue
-        for n, v in zip(names, f[5:9]):
-            if v.lower() == "active":
-                reasons.add(n)
-    os.unlink(path)
-    if not sms:
-        return None
-    load = [s for s in sms if mx and s > 0.5 * mx] or sms
-    return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": sorted(reasons),
-            "samples": len(sms)}
-
+# ---------------------------------------------------------------------------
+# baselines on the host cores and the reference's own paths
+# ---------------------------------------------------------------------------
 
 def cpu_baseline(workload, max_seconds=20.0):
-    """Time the oracle port (test infrastructure, used only as this baseline)
-    on a bounded row sample of the workload; returns the baseline dict."""
+    """Time the C restatement of the reference's algorithm (test
+    infrastructure, used only as this baseline) on a bounded row sample of
+    the workload; returns the baseline dict."""
     import numpy as np
     import torch
     from oracle import sc_oracle as O
@@ -152,7 +212,7 @@ def cpu_baseline(workload, max_seconds=20.0):
     try:
         from oracle import c_oracle as CO
         have_c = CO.available()
-    except Exception:
+    except Exception:  # noqa: BLE001
         have_c = False
     g = torch.Generator().manual_seed(0)
     if workload == "config5":
@@ -167,27 +227,50 @@ def cpu_baseline(workload, max_seconds=20.0):
     an, bn = a.numpy(), b.numpy()
     q = dict(p)
     gran = q.pop("granularity")
-    rows = 8
-    while True:
+
+    def call(rows):
         sa, sb = np.ascontiguousarray(an[..., :rows, :]), np.ascontiguousarray(bn[..., :rows, :])
         t0 = time.perf_counter()
         if have_c:
             CO.sc_matmul(sa, sb, gran, threads=threads, **q)
         else:
             O.sc_matmul(sa, sb, gran, env={}, **q)
-        dt = time.perf_counter() - t0
+        return time.perf_counter() - t0
+
+    # untimed first call: sequences and tables are built once per key and
+    # cached, as the reference's RNG and table caches keep them
+    call(8)
+    rows = 8
+    while True:
+        dt = call(rows)
         if dt > max_seconds / 4 or rows >= an.shape[-2]:
             break
         rows = min(an.shape[-2], rows * 2)
     bh = a.shape[0] if a.dim() == 3 else 1
     ops = 2.0 * bh * rows * rows * D
     return {"value": ops / dt / 1e9, "unit": "GOPS", "cores": threads if have_c else 1,
-            "kind": "port", "sample": f"{gran} {workload} slice: {bh}x{rows}x{rows}x{D} (L={L}) in {dt:.2f}s, "
-                                      f"{'C oracle, OpenMP' if have_c else 'numpy oracle, 1 thread'}"}
+            "kind": "port", "bit_ops_per_s": ops / 2 * L / dt,
+            "sample": f"{gran} {workload} slice: {bh}x{rows}x{rows}x{D} (L={L}) in {dt:.2f}s, "
+                      f"{'C restatement, OpenMP' if have_c else 'numpy restatement, 1 thread'}"}
+
+
+def reference_run(mode: str, timeout_s: float, budget_s: float = 60.0):
+    """One of baseline/reference_runs.py's measurements in a subprocess."""
+    cmd = [sys.executable, os.path.join(REPO, "baseline", "reference_runs.py"), mode, "--budget-s", str(budget_s)]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout_s)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"did not finish within {timeout_s:.0f} s"}
+    for line in reversed(r.stdout.strip().splitlines()):
+        try:
+            return json.loads(line)
+        except ValueError:
+            continue
+    return {"unavailable": f"exit {r.returncode}: {(r.stderr or r.stdout).strip()[-300:]}"}
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the oracle port on the host cores, rank 0 only."""
+    """--impl reference: the C restatement on the host cores, rank 0 only."""
     if rank != 0:
         return
     base = cpu_baseline(args.workload, max_seconds=max(5.0, 60.0 / max(1, args.steps + args.warmup)))
@@ -201,50 +284,38 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def main():
-    args = parse()
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.impl == "reference":
-        return run_reference(args, rank, world)
+# ---------------------------------------------------------------------------
+# one workload, timed
+# ---------------------------------------------------------------------------
 
+def measure(name, shape, args, rank, world, dev, sampler=None, check_rows=128):
     import torch
     import torch.distributed as dist
     from scmp_kernels_b200 import _lib, sc_matmul
+    from scmp_kernels_b200 import dist as SD
 
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+    a, b_full, s, kw, (BH, N, M, D), L = build_workload(name, dev, shape)
+    lo, hi = (0, M)
+    b = b_full
     if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-
-    shape = tuple(int(x) for x in args.shape.split(",")) if args.shape else None
-    a, b, s, kw, (BH, N, M, D), L = build_workload(args.workload, dev, shape)
-    # shard the weight operand by rows
-    if world > 1:
-        rows = b.shape[-2]
-        per = (rows + world - 1) // world
-        b = b[..., rank * per:min(rows, (rank + 1) * per), :].contiguous()
+        lo, hi = SD.shard_bounds(M, world, rank)
+        b = b_full[..., lo:hi, :].contiguous()
     kw = dict(kw)
     if s is not None:
         kw["smooth_scales"] = s
     calls = [(None, kw)]
-    if args.workload == "config4":
+    if name == "config4":
         from scmp_kernels_b200 import workloads as W
         lv = W.mp_row_levels(a, 4, (256, 128, 64))
         calls = [(rows_.to(dev), dict(kw, stoc_len=Lv, rng_levels=Lv)) for Lv, rows_ in lv.items()]
     a_parts = [a if idx is None else a[idx].contiguous() for idx, _ in calls]
 
-    from scmp_kernels_b200 import dist as SD
-
     def one_call(ai, b_, ci):
-        if world > 1:  # this rank's column block, all-gathered into the full output
-            return SD.sc_matmul_sharded(ai, b_, M, **ci)
+        if world > 1:  # this rank's column block, stored into every rank's output
+            return SD.sc_matmul_sharded(ai, b_, M, copy=False, **ci)
         return sc_matmul(ai, b_, **ci)
 
-    def step(a_list=a_parts, b_=b):
-        ys = [one_call(ai, b_, ci) for ai, (_, ci) in zip(a_list, calls)]
+    def assemble(ys):
         if len(ys) == 1:
             return ys[0]
         y = torch.empty(a.shape[:-1] + (M,), dtype=torch.float32, device=dev)
@@ -252,91 +323,106 @@ def main():
             y[idx] = yi
         return y
 
-    # rank 0's GPU is sampled from warm-up to the end of the timed steps (the
-    # line reports rank 0's clocks); the other GPUs are not polled, since an
-    # nvidia-smi query can briefly stall a GPU and the per-call barrier of the
-    # sharded path would pass every rank's stall on to all of them
-    clk_p, clk_f = clocks_start(local) if rank == 0 else (None, None)
-    if clk_p is not None:
-        clocks_wait_first_sample(clk_f)
     for _ in range(args.warmup):
-        step()
+        assemble([one_call(ai, b, ci) for ai, (_, ci) in zip(a_parts, calls)])
     torch.cuda.synchronize()
 
-    # GEMM-only timing through the library's profiling hook
     L_ = _lib.lib()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps * len(calls))]
-    for e0, e1 in ev:  # torch creates the CUDA event on first record
+    nev = args.steps * len(calls)
+    mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    gev = [(mk(), mk()) for _ in range(nev)]
+    qev = [(mk(), mk()) for _ in range(nev)]
+    for e0, e1 in gev + qev:  # torch creates the CUDA event on first record
         e0.record()
         e1.record()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler is not None:
+        sampler.start()
+    t0, t1 = mk(), mk()
     launches0 = _lib.launch_count()
     t0.record()
     ei = 0
     for _ in range(args.steps):
         ys = []
         for ai, (_, ci) in zip(a_parts, calls):
-            L_.scmp_set_profile_events(ev[ei][0]._as_parameter_, ev[ei][1]._as_parameter_)
+            L_.scmp_set_profile_events(gev[ei][0]._as_parameter_, gev[ei][1]._as_parameter_)
+            L_.scmp_set_quant_profile_events(qev[ei][0]._as_parameter_, qev[ei][1]._as_parameter_)
             ys.append(one_call(ai, b, ci))
             ei += 1
         L_.scmp_set_profile_events(None, None)
-        if len(ys) > 1:
-            y = torch.empty(a.shape[:-1] + (M,), dtype=torch.float32, device=dev)
-            for (idx, _), yi in zip(calls, ys):
-                y[idx] = yi
-        else:
-            y = ys[0]
+        L_.scmp_set_quant_profile_events(None, None)
+        y = assemble(ys)
     t1.record()
     torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler is not None else None
     launches = _lib.launch_count() - launches0
-    clocks = clocks_stop(clk_p, clk_f)
     ms = t0.elapsed_time(t1) / args.steps
-    gemm_ms = sum(e0.elapsed_time(e1) for e0, e1 in ev) / args.steps
+    gemm_ms = sum(e0.elapsed_time(e1) for e0, e1 in gev) / args.steps
+    quant_ms = sum(e0.elapsed_time(e1) for e0, e1 in qev) / args.steps
     if world > 1:
-        tt = torch.tensor([ms, gemm_ms], device=dev)
+        tt = torch.tensor([ms, gemm_ms, quant_ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms, gemm_ms = tt.tolist()
+        ms, gemm_ms, quant_ms = tt.tolist()
     assert _lib.device_error() == 0, "device-side error during the bench"
 
     ops = 2.0 * BH * N * M * D
-    value = ops / (ms * 1e-3) / 1e9
+    Lw = L if L is not None else 149.33
+    res = {"workload": name, "desc": WORKLOADS[name], "value": ops / (ms * 1e-3) / 1e9, "unit": "GOPS",
+           "ms_per_step": ms, "gemm_ms_per_step": gemm_ms, "quant_ms_per_step": quant_ms,
+           "bit_ops_per_s": ops / 2 * Lw / (ms * 1e-3), "gpu_launches": launches, "clocks": clocks,
+           "_tensor_ops_per_rank": 2.0 * BH * N * (hi - lo) * D * Lw}
+    # quantiser: read 4 B per element of a and b, write its 2-byte operand
+    # (the row statistics and scales are O(rows))
+    res["_quant_bytes"] = 6.0 * BH * (N + (hi - lo)) * D
 
-    # end-to-end through the public API from pinned host memory
-    e2e = None
+    # multi-GPU: the gathered output against single-GPU row slices
+    if world > 1 and len(calls) == 1 and BH == 1:
+        rows = sorted(set(range(min(check_rows, N))) | set(range(max(0, N - check_rows), N)))
+        idx = torch.tensor(rows, device=dev)
+        ok_t = torch.ones(1, device=dev)
+        ref = sc_matmul(a[idx].contiguous(), b_full, **kw)
+        if not torch.equal(y[idx], ref):
+            ok_t.zero_()
+        dist.all_reduce(ok_t, op=dist.ReduceOp.MIN)
+        res["check"] = {"bit_exact": bool(ok_t.item() == 1), "rows": len(rows),
+                        "how": "every rank's gathered output vs single-GPU sc_matmul of those rows of a "
+                               "against the whole of b"}
+    del y
+
+    # end to end through the public API from pinned host memory
     if not args.no_e2e:
         ha = [x.cpu().pin_memory() for x in a_parts]
         hb = b.cpu().pin_memory()
         hs = s.cpu().pin_memory() if s is not None else None
-        hy = torch.empty(y.shape, dtype=torch.float32).pin_memory()
         n_e2e = max(1, min(args.steps, 5))
-        if world == 1 and len(calls) == 1:
-            # the public API on pinned host operands: it streams b to the
-            # device and the result back in blocks while it computes
+        out_bytes = N * (hi - lo) * 4 * BH
+        if len(calls) == 1:
             ci_host = dict(calls[0][1])
             if hs is not None:
                 ci_host["smooth_scales"] = hs
-
-            def e2e_step():  # returns the result in pinned host memory
-                return sc_matmul(ha[0], hb, **ci_host)
+            if world > 1:
+                def e2e_step():  # this rank's column block back to host memory, no gather
+                    return SD.sc_matmul_sharded(ha[0], hb, M, gather=False, **ci_host)
+            else:
+                def e2e_step():  # streamed host path; result in pinned host memory
+                    return sc_matmul(ha[0], hb, **ci_host)
         else:
+            hy = torch.empty(a.shape[:-1] + ((hi - lo) if world > 1 else M,), dtype=torch.float32).pin_memory()
+
             def e2e_step():
                 da = [x.to(dev, non_blocking=True) for x in ha]
                 db = hb.to(dev, non_blocking=True)
-                if hs is not None:
-                    for _, ci in calls:
-                        ci["smooth_scales"] = hs.to(dev, non_blocking=True)
-                yy = step(da, db)
-                hy.copy_(yy, non_blocking=True)
+                ys = [SD.sc_matmul_sharded(ai, db, M, gather=False, **ci) if world > 1 else sc_matmul(ai, db, **ci)
+                      for ai, (_, ci) in zip(da, calls)]
+                hy.copy_(assemble(ys), non_blocking=True)
         e2e_step()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, e1 = mk(), mk()
         e0.record()
         for _ in range(n_e2e):
             e2e_step()
@@ -348,59 +434,124 @@ def main():
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             e_ms = tt.item()
         bi = sum(x.numel() * 4 for x in ha) + hb.numel() * 4 + (hs.numel() * 4 if hs is not None else 0)
-        e2e = {"value": ops / (e_ms * 1e-3) / 1e9, "unit": "GOPS", "h2d_bytes_per_step": bi,
-               "d2h_bytes_per_step": hy.numel() * 4, "ms_per_step": e_ms}
+        res["e2e"] = {"value": ops / (e_ms * 1e-3) / 1e9, "unit": "GOPS", "h2d_bytes_per_step": bi,
+                      "d2h_bytes_per_step": out_bytes, "ms_per_step": e_ms,
+                      "output": ("each rank's column block of the result to its host memory (the result "
+                                 "stays sharded by columns)") if world > 1 else "the whole result"}
+    del a, b, b_full, a_parts
+    torch.cuda.empty_cache()
+    return res
+
+
+def roofline_of(res, args, world, peaks, src, shape):
+    """Tensor-core roofline of the GEMM kernel and HBM roofline of the quantiser."""
+    bf16 = peaks.get("bf16_tflops", 1590.0)
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    env = os.environ
+    L = {"config5": 64}.get(res["workload"], 256 if res["workload"] != "config4" else None)
+    e2m1 = (env.get("SCMP_TC_INT8") != "1" and env.get("SCMP_TC_ATMEM") != "1"
+            and env.get("SCMP_TC_SINGLE") != "1" and (L is None or L > 32))
+    kind = "e2m1" if e2m1 else "int8"
+    tc_peak = (4.0 if e2m1 else 2.0) * bf16
+    achieved = res["_tensor_ops_per_rank"] / (res["gemm_ms_per_step"] * 1e-3) / 1e12
+    roof = {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": f"TOPS ({kind})",
+            "frac": achieved / tc_peak,
+            "traffic": (GEMM_TRAFFIC_BYTES.get(res["workload"]) if shape is None and world == 1 else None),
+            "peak_source": f"{'4' if e2m1 else '2'} x bf16_tflops of {src} peaks (dense {kind} = "
+                           f"{'4' if e2m1 else '2'} x dense bf16)"}
+    clk = res.get("clocks") or {}
+    if clk.get("sm_mhz"):
+        nominal = B200_SMS * MACS_PER_SM_CLK[kind] * 2 * clk["sm_mhz"] * 1e6 / 1e12
+        roof["nominal_at_sampled_clock"] = nominal
+        roof["frac_of_nominal_at_sampled_clock"] = achieved / nominal
+    q_gbs = res["_quant_bytes"] / (res["quant_ms_per_step"] * 1e-3) / 1e9 if res["quant_ms_per_step"] > 0 else None
+    quant = {"bound": "hbm", "achieved": q_gbs, "peak": hbm, "unit": "GB/s",
+             "frac": (q_gbs / hbm) if q_gbs else None, "bytes_per_step": res["_quant_bytes"],
+             "ms_per_step": res["quant_ms_per_step"],
+             "what": "operand preparation per step (row statistics, quantisers, padded row map): "
+                     "4 B read + 2 B written per element of a and of this rank's b"}
+    return roof, quant
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from scmp_kernels_b200 import dist as SD
+
+    shape = tuple(int(x) for x in args.shape.split(",")) if args.shape else None
+    # rank 0's GPU is sampled during each timed region (the line reports rank
+    # 0's clocks); the other GPUs are not polled
+    sampler = ClockSampler(local) if rank == 0 else None
+    head = measure(args.workload, shape, args, rank, world, dev, sampler)
+    sides = []
+    if args.side and args.side != "none" and shape is None:
+        for w in args.side.split(","):
+            if w and w != args.workload:
+                sides.append(measure(w, None, args, rank, world, dev, sampler))
+    failed = [r["workload"] for r in [head] + sides if r.get("check") and not r["check"]["bit_exact"]]
 
     if rank == 0:
-        peaks = {}
+        peaks, src = {}, "fallback"
         try:
             peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
             src = "measured"
         except OSError:
-            src = "fallback"
-        bf16 = peaks.get("bf16_tflops", 1590.0)
-        # The SC-GEMM is a GEMM over K = D*L with operands in {-1, 0, 1} (sign x
-        # thermometer, sign x stream). SM pairs run it on e2m1 operands
-        # (kind::mxf4, dense rate 4x bf16) for streams of 64 positions or more,
-        # else on int8 operands (kind::i8, dense rate 2x bf16).
-        env = os.environ
-        e2m1 = (env.get("SCMP_TC_INT8") != "1" and env.get("SCMP_TC_ATMEM") != "1"
-                and env.get("SCMP_TC_SINGLE") != "1" and (L is None or L > 32))
-        tc_peak = (4.0 if e2m1 else 2.0) * bf16
-        tc_unit = "TOPS (e2m1)" if e2m1 else "TOPS (int8)"
-        tc_src = (f"4 x bf16_tflops of {src} peaks (dense e2m1 = 4 x dense bf16)" if e2m1 else
-                  f"2 x bf16_tflops of {src} peaks (dense int8 = 2 x dense bf16)")
-        Lw = L if L is not None else 149.33
-        tensor_ops = 2.0 * BH * N * (M // world if world > 1 else M) * D * Lw
-        achieved = tensor_ops / (gemm_ms * 1e-3) / 1e12
+            pass
+        roof, quant = roofline_of(head, args, world, peaks, src, shape)
+        e2m1 = roof["unit"].endswith("(e2m1)")
         line = {
-            "metric": "SC-GEMM equiv GOPS (2*BH*N*M*D/s)", "value": value, "unit": "GOPS",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "metric": "SC-GEMM equiv GOPS (2*BH*N*M*D/s)", "value": head["value"], "unit": "GOPS",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "e2m1xe2m1->f32 (exact integer sums)" if e2m1 else "int8xint8->int32",
             "data": "synthetic (seeded, reference shapes and distributions)",
             "config": {"workload": args.workload, "desc": WORKLOADS[args.workload],
                        "l2": "inputs larger than L2 (b is 180 MB fp32)" if args.workload == "config2" else
                        "per-step operands re-read from HBM",
-                       "parallelism": f"b sharded by rows x{world}, NCCL all-gather of outputs" if world > 1
+                       "parallelism": (f"b sharded by rows x{world}, each rank's block stored into every "
+                                       f"rank's output by the GEMM epilogue (NVLink)") if world > 1
                        else "single GPU"},
-            "gpu_launches": launches,
-            "gemm_ms_per_step": gemm_ms,
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": tc_unit,
-                         "frac": achieved / tc_peak,
-                         "traffic": (GEMM_TRAFFIC_BYTES.get(args.workload) if shape is None and world == 1
-                                     else None),
-                         "peak_source": tc_src},
-            "clocks": clocks,
-            "e2e": e2e,
+            "gpu_launches": head["gpu_launches"],
+            "gemm_ms_per_step": head["gemm_ms_per_step"],
+            "bit_ops_per_s": head["bit_ops_per_s"],
+            "roofline": roof,
+            "quant_roofline": quant,
+            "clocks": head["clocks"],
+            "e2e": head.get("e2e"),
         }
+        if "check" in head:
+            line["check"] = head["check"]
+        for r in sides:
+            r_roof, r_quant = roofline_of(r, args, world, peaks, src, None)
+            line[r["workload"]] = {k: v for k, v in r.items() if not k.startswith("_")}
+            line[r["workload"]]["roofline"] = r_roof
+            line[r["workload"]]["quant_roofline"] = r_quant
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.workload)
+        if world == 1 and not args.no_reference_runs and shape is None:
+            line["reference_gpu"] = reference_run("gpu", timeout_s=300, budget_s=60)
+            line["cpu_baseline_interpreter"] = reference_run("interp", timeout_s=300)
         print(json.dumps(line), flush=True)
     if world > 1:
         SD.release_peer_buffers()
         dist.barrier()
         dist.destroy_process_group()
+    if failed:
+        sys.stderr.write(f"bench: multi-GPU output check failed for {failed}\n")
+        sys.exit(3)
 
 
 if __name__ == "__main__":

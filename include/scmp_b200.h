@@ -12,8 +12,10 @@
  *     never throws or aborts; scmp_last_error() gives a message for the
  *     calling thread;
  *   - all array pointers are device pointers owned by the caller unless the
- *     parameter says "host"; nothing here allocates device memory except the
- *     one-time error flag of scmp_device_error();
+ *     parameter says "host"; the compute entry points allocate no device
+ *     memory (scratch comes from the caller's workspace, or from the fixed
+ *     array of scmp_sc_matmul_noalloc); scmp_peer_alloc is the one function
+ *     that allocates (with cudaMalloc), and scmp_peer_free releases it;
  *   - work is enqueued on the given CUDA stream (a cudaStream_t passed as
  *     void*; NULL is the legacy default stream) on the current device;
  *   - float arithmetic follows the reference bit for bit: IEEE float32 with
@@ -250,6 +252,11 @@ int scmp_grouped_asymmetric_quant(const float* x, int rows, int cols, int group,
  * gemm_stop right after it, so a caller can time the GEMM kernel alone. Both
  * are cudaEvent_t passed as void*; NULL, NULL turns the hook off. Process-wide. */
 int scmp_set_profile_events(void* gemm_start, void* gemm_stop);
+/* The same for the operand preparation of scmp_sc_matmul: quant_start is
+ * recorded before its first kernel (row statistics, quantisers, the padded
+ * row map) and quant_stop after its last, before the SC-GEMM; NULL, NULL
+ * turns it off. Process-wide. */
+int scmp_set_quant_profile_events(void* quant_start, void* quant_stop);
 
 /* Diagnostics. scmp_device_error synchronises the device, returns in *code
  * the first error a kernel recorded since the last call (SCMP_OK if none)

@@ -405,10 +405,20 @@ def smooth(a: np.ndarray, b: np.ndarray, s: np.ndarray):
 # path orchestrators  (scmp_kernels/sc/kernels.py, scmp_kernels/sc/matmul.py)
 # ---------------------------------------------------------------------------
 
+_TABLES_CACHE: dict = {}
+
+
 def _tables(config, D, sc_prec, stoc_len, G, env):
+    """Tables of one key, kept like the reference's RNG and table caches
+    (kernels.py:59-87, 762-777), with the environment in the key."""
     if config is None:
         config = make_sobol_simple_config(D, D, sc_prec)
-    return Tables(config, sc_prec, stoc_len, G, env)
+    key = (json.dumps(config, sort_keys=True), sc_prec, stoc_len, G,
+           json.dumps(env if env is not None else dict(os.environ), sort_keys=True))
+    t = _TABLES_CACHE.get(key)
+    if t is None:
+        t = _TABLES_CACHE[key] = Tables(config, sc_prec, stoc_len, G, env)
+    return t
 
 
 def per_tensor(a, b, mode, sc_prec, config, stoc_len, rng_levels, env=None):

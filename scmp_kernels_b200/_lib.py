@@ -53,6 +53,7 @@ SIGNATURES = {
     "scmp_abi_version": (c_int, []),
     "scmp_launch_count": (ctypes.c_ulonglong, []),
     "scmp_set_profile_events": (c_int, [c_void_p, c_void_p]),
+    "scmp_set_quant_profile_events": (c_int, [c_void_p, c_void_p]),
     "scmp_last_error": (ctypes.c_char_p, []),
     "scmp_device_error": (c_int, [ctypes.POINTER(c_int)]),
     "scmp_build_tables": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p,

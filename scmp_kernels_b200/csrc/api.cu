@@ -10,6 +10,7 @@ namespace scmp {
 
 static thread_local std::string t_last_error;
 static cudaEvent_t g_prof_start = nullptr, g_prof_stop = nullptr;
+static cudaEvent_t g_qprof_start = nullptr, g_qprof_stop = nullptr;
 
 // Copy of the dimension -> table-row map padded with zeros to 8*ceil(d/8),
 // so the GEMM can read it in aligned blocks of eight.
@@ -188,6 +189,12 @@ int scmp_set_profile_events(void* gemm_start, void* gemm_stop) {
   return SCMP_OK;
 }
 
+int scmp_set_quant_profile_events(void* quant_start, void* quant_stop) {
+  g_qprof_start = (cudaEvent_t)quant_start;
+  g_qprof_stop = (cudaEvent_t)quant_stop;
+  return SCMP_OK;
+}
+
 const char* scmp_last_error(void) { return t_last_error.c_str(); }
 
 int scmp_device_error(int* code) {
@@ -301,6 +308,7 @@ int scmp_sc_matmul(const scmp_matmul_desc* d, void* workspace, size_t workspace_
   g.pattern = d->pattern;
   g.pattern4 = d->pattern4;
   g.bmap = p.bmap;
+  if (g_qprof_start) cudaEventRecord(g_qprof_start, st);
   SCMP_CUDA(launch_pad_map(d->bmap, d->d, p.bmap, st), "pad bmap");
   g.unit_d = d->d;
   if (d->n_out_peers > 0) {
@@ -406,6 +414,7 @@ int scmp_sc_matmul(const scmp_matmul_desc* d, void* workspace, size_t workspace_
     g.epi.bsum = p.sum_b;
   }
 
+  if (g_qprof_stop) cudaEventRecord(g_qprof_stop, st);
   SCMP_CUDA(launch_gemm(g, d->flags, st), "sc_gemm");
   return SCMP_OK;
 }

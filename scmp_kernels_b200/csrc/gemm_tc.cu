@@ -1035,12 +1035,12 @@ template <int TLEN, int SPD, bool PAIR, bool ATMEM = false, bool WIDE = ATMEM &&
           bool UNR = F4 && WIDE>
 static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int sms, cudaStream_t st) {
   using C = Cfg<PAIR, ATMEM, WIDE, F4>;
-  static bool attr = false;
   auto kern = gemm_tc_kernel<TLEN, SPD, PAIR, ATMEM, WIDE, F4, UNR>;
-  if (!attr) {
+  // The attribute belongs to the current device's context, so it is set on
+  // every launch (a host call; a process may drive several devices).
+  {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    attr = true;
   }
   if constexpr (!PAIR) {
     const int grid = s.workers;

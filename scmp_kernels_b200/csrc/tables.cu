@@ -56,8 +56,10 @@ cudaError_t launch_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, 
                                 cudaStream_t st) {
   const size_t sm = (size_t)L * sizeof(int32_t);
   if (sm > 48 * 1024) {
-    cudaFuncSetAttribute(k_table_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    cudaFuncSetAttribute(pattern_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    cudaError_t e = cudaFuncSetAttribute(k_table_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(pattern_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) return e;
   }
   if (n_ra > 0) {
     k_table_kernel<<<n_ra, 256, sm, st>>>(ra, L, vcap, ktab);

@@ -99,7 +99,17 @@ class _PeerOutputs:
         self.own, self.opened, self.slots = [], [], []
 
 
+# Buffers per (group members and backend, output shape, device). Keyed by the
+# members rather than the group object, so that a group destroyed and another
+# created in its place (possibly at the same address) never inherits mappings
+# made for different ranks; groups with the same members share the buffers,
+# which is safe because every call ends with a barrier over those members.
 _PEER_OUTPUTS: dict = {}
+
+
+def _group_key(group):
+    return (tuple(dist.get_process_group_ranks(group if group is not None else dist.group.WORLD)),
+            str(dist.get_backend(group)))
 
 
 def release_peer_buffers(group=None) -> None:
@@ -127,11 +137,12 @@ def _use_fused(a: torch.Tensor, group, world: int, matmul) -> bool:
             and dist.get_backend(group) == "nccl")
 
 
-def _fused(a, shape, offset: int, ld: int, group, compute):
+def _fused(a, shape, offset: int, ld: int, group, compute, copy: bool = True):
     """Run ``compute()`` with its result scattered into every rank's buffer of
-    ``shape`` at ``offset`` / ``ld``; return this rank's copy of the full result."""
+    ``shape`` at ``offset`` / ``ld``; return this rank's copy of the full result
+    (with ``copy=False`` the library's buffer itself, see sc_matmul_sharded)."""
     from .sc import kernels as K
-    key = (id(group), tuple(shape), a.device.index)
+    key = (_group_key(group), tuple(shape), a.device.index)
     po = _PEER_OUTPUTS.get(key)
     if po is None:
         po = _PEER_OUTPUTS[key] = _PeerOutputs(shape, a.device, group)
@@ -140,13 +151,20 @@ def _fused(a, shape, offset: int, ld: int, group, compute):
         compute()
     # every rank's epilogue has stored its block once this collective completes
     dist.all_reduce(torch.zeros(1, device=a.device), group=group)
-    return view.clone()
+    return view.clone() if copy else view
+
+
+def _collective_device(group, like: torch.Tensor) -> torch.device:
+    """Where a small tensor for a collective of ``group`` must live."""
+    if dist.get_backend(group) == "nccl":
+        return like.device if like.is_cuda else torch.device("cuda", torch.cuda.current_device())
+    return torch.device("cpu")
 
 
 def sc_matmul_sharded(a: torch.Tensor, b_shard: torch.Tensor, rows_total: int,
                       granularity: str = "per_row", *, group=None,
                       matmul: Optional[Callable] = None, fused: Optional[bool] = None,
-                      **kw) -> torch.Tensor:
+                      gather: bool = True, copy: bool = True, **kw) -> torch.Tensor:
     """``sc_matmul(a, b)`` with ``b`` sharded by rows over the process group.
 
     a: replicated ``(N, D)`` (or ``(BH, N, D)``); b_shard: this rank's rows of
@@ -154,12 +172,21 @@ def sc_matmul_sharded(a: torch.Tensor, b_shard: torch.Tensor, rows_total: int,
     ``sc_matmul`` keyword arguments. ``matmul`` replaces the per-rank compute
     (the default is this package's ``sc_matmul``); ``fused`` selects the
     epilogue all-gather (default: NCCL groups of up to 8 ranks).
+
+    gather=False returns only this rank's ``(..., N, M_r)`` column block, with
+    no all-gather (the output stays sharded, as a tensor-parallel consumer
+    takes it); operands in pinned host memory then take sc_matmul's streamed
+    host path and the block comes back in pinned host memory.
+
+    copy=False (fused path) returns the library's gather buffer itself
+    instead of a copy: it holds the result until the second-next fused call
+    of the same output shape on this group overwrites it.
     """
     world = dist.get_world_size(group)
     if granularity == "per_head":
         raise ValueError("sc_matmul_sharded: per_head is sharded by heads, use sc_matmul_sharded_heads")
     if fused is None:
-        fused = _use_fused(a, group, world, matmul)
+        fused = gather and _use_fused(a, group, world, matmul)
     ranges = None
     if granularity == "per_tensor":
         # quantisation uses b's global range (of the smoothed operand when
@@ -171,6 +198,7 @@ def sc_matmul_sharded(a: torch.Tensor, b_shard: torch.Tensor, rows_total: int,
             r = torch.stack([bs.amax(), -bs.amin()]).to(torch.float32)
         else:
             r = torch.full((2,), float("-inf"), device=bs.device)
+        r = r.to(_collective_device(group, bs))
         dist.all_reduce(r, op=dist.ReduceOp.MAX, group=group)
         ranges = dict(max_fp_a=float(aa.max()), min_fp_a=float(aa.min()),
                       max_fp_b=float(r[0]), min_fp_b=-float(r[1]))
@@ -194,6 +222,8 @@ def sc_matmul_sharded(a: torch.Tensor, b_shard: torch.Tensor, rows_total: int,
                                      config=kw.get("config"), stoc_len=stoc_len, rng_levels=rng_levels,
                                      smooth_scales=kw.get("smooth_scales"))
 
+    if not gather:
+        return compute()
     if not fused:
         return _all_gather_cols(compute(), rows_total, world, group)
     rank = dist.get_rank(group)
@@ -201,7 +231,7 @@ def sc_matmul_sharded(a: torch.Tensor, b_shard: torch.Tensor, rows_total: int,
     if b_shard.shape[-2] != hi - lo:
         raise ValueError(f"sc_matmul_sharded: rank {rank} holds {b_shard.shape[-2]} rows of b, "
                          f"shard_bounds gives {hi - lo}")
-    return _fused(a, (*a.shape[:-1], rows_total), lo, rows_total, group, compute)
+    return _fused(a, (*a.shape[:-1], rows_total), lo, rows_total, group, compute, copy)
 
 
 def sc_matmul_sharded_heads(a_shard: torch.Tensor, b_shard: torch.Tensor, heads_total: int, *,

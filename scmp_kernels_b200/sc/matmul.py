@@ -188,6 +188,10 @@ def _per_row_host_pipelined(a: torch.Tensor, b: torch.Tensor, run, group_a: int,
     out_host = torch.empty((n, m), dtype=torch.float32, pin_memory=True)
     for t, st in ((a_dev, comp), (b_dev, comp), (out_dev, s_out)):
         t.record_stream(st)
+    # The staging buffers come from the caller's stream's pool: a block freed
+    # there may still be in use by work queued on it, so the copy stream
+    # starts after that work.
+    s_in.wait_stream(comp)
     # copies in the order they are needed: a's first block, b's blocks, a's other blocks
     ev_b = []
     with torch.cuda.stream(s_in):

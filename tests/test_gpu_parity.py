@@ -246,6 +246,34 @@ def test_host_operands_pipelined_equal_device_result(kw, env_vars):
     assert _lib.device_error() == 0
 
 
+def test_host_pipelined_waits_for_work_queued_on_freed_blocks(env_vars):
+    """The streamed path's device staging buffers come from the caller's
+    stream's memory pool; a block freed there may still be written by work
+    queued on that stream. The copies into the staging buffers run on another
+    stream and must start only after that work: here a spin kernel delays
+    writes of huge values into two freed tensors of the staging buffers'
+    sizes, and the result must still equal the device call's."""
+    env_vars({})
+    from scmp_kernels_b200.sc import matmul as MM
+    g = torch.Generator().manual_seed(8)
+    n, m, d = MM._HOST_MIN_ROWS + 77, MM._HOST_MIN_ROWS + 333, 256
+    a = torch.randn(n, d, generator=g).pin_memory()
+    b = (torch.randn(m, d, generator=g) * 0.05).pin_memory()
+    ref = sc_matmul(a.to(DEV), b.to(DEV), "per_row", sc_prec=8).cpu()
+    junk_a = torch.full((n, d), 1e30, device=DEV)
+    junk_b = torch.full((m, d), -1e30, device=DEV)
+    for _ in range(3):
+        x = torch.empty(n, d, device=DEV)
+        y = torch.empty(m, d, device=DEV)
+        torch.cuda._sleep(20_000_000)  # a bounded spin (about 10 ms) on the current stream
+        x.copy_(junk_a)
+        y.copy_(junk_b)
+        del x, y
+        out = sc_matmul(a, b, "per_row", sc_prec=8)
+        assert torch.equal(out, ref)
+    assert _lib.device_error() == 0
+
+
 def test_native_kernels_do_the_work():
     """One per_row call launches the library's own kernels: two quantisers,
     the padded row map and the SC-GEMM."""
