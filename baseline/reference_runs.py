@@ -98,14 +98,69 @@ def run_gpu(budget_s: float) -> None:
     torch.cuda.synchronize()
     mism = int((y_ref != y_ours).sum().item())
     ops = 2.0 * rows * m * d
-    print(json.dumps({
+    line = {
         "value": ops / (ms * 1e-3) / 1e9, "unit": "GOPS", "ms_per_call": ms, "rows_of_a": rows,
         "workload": "config2" if rows == n else f"config2, first {rows} of {n} rows of a",
         "calls_timed": reps, "cold_first_call_s": cold_s,
         "triton": triton.__version__, "torch": torch.__version__,
         "kernel": "enable_matmul_tiled_kernel (reference default table path)",
-        "bit_exact_vs_ours": mism == 0, "mismatches": mism, "elements_compared": rows * m,
-    }), flush=True)
+        "end_to_end": {"bit_exact_vs_ours": mism == 0, "mismatches": mism, "elements_compared": rows * m},
+    }
+    del y_ref, y_ours
+    line["gemm_kernel"] = _compare_gemm_kernels(xa, b)
+    line["row_scales"] = _compare_row_scales(xa, b)
+    print(json.dumps(line), flush=True)
+
+
+def _compare_gemm_kernels(xa, b):
+    """The reference's GEMM kernel (enable_matmul_triton) and this library's
+    (scmp_enable_matmul) on the same quantised operands: the reference's own
+    quantisation of a and b on this GPU."""
+    import torch
+    import scmp_kernels.sc.kernels as RK
+    from scmp_kernels.quant.grouped import _grouped_symmetric_quant as ref_gq
+    from scmp_kernels.sc.config_helpers import make_sobol_simple_config as ref_cfg
+    from scmp_kernels_b200.sc import kernels as K
+    from scmp_kernels_b200.sc.config_helpers import make_sobol_simple_config
+    n, d = xa.shape
+    m = b.shape[0]
+    q, G, L = 127, 256, 256
+    _, a_int, sign_a = ref_gq(xa, 1, q)
+    _, b_int, sign_b = ref_gq(b, 1, q)
+    ba = (a_int.abs() * G / q).round().short()
+    bb = (b_int.abs() * G / q).round().short()
+    cfg = ref_cfg(d, d, 8)
+    ra, rb = RK._get_cached_sequences(cfg, 8, xa.device)
+    cum, kt = RK._get_cached_enable_tables(cfg, 8, xa.device, ra, rb, L, rng_levels=G)
+    raw_ref = RK.enable_matmul_triton(cum, kt, ba, bb, sign_a, sign_b, n, m, d, L, float(q * q), True)
+    del cum
+    t = K._get_cached_enable_tables(make_sobol_simple_config(d, d, 8), 8, xa.device, L, G)
+    raw_ours = K.enable_matmul(t, ba, bb, sign_a, sign_b, n, m, d, L, float(q * q), True)
+    torch.cuda.synchronize()
+    mism = int((raw_ref != raw_ours).sum().item())
+    return {"bit_exact": mism == 0, "mismatches": mism, "elements_compared": n * m,
+            "what": "fl32(S * q_max^2 / L) of enable_matmul_triton vs scmp_enable_matmul on the reference's "
+                    "own boundaries and signs of a and b"}
+
+
+def _compare_row_scales(xa, b):
+    """The per-row scale absmax / q_max of the reference's grouped quantiser,
+    as torch evaluates it on this GPU and on the CPU (which the interpreter
+    runs, and which the fixtures and this library follow)."""
+    import torch
+    from scmp_kernels.quant.grouped import _grouped_symmetric_quant as ref_gq
+    out = {}
+    for name, x in (("a", xa), ("b", b)):
+        s_gpu, i_gpu, _ = ref_gq(x, 1, 127)
+        s_cpu, i_cpu, _ = ref_gq(x.cpu(), 1, 127)
+        amax = x.abs().amax(dim=1).clamp(min=1e-5).cpu()
+        recip = amax * torch.tensor(1.0 / 127, dtype=torch.float32)
+        out[name] = {"rows": int(x.shape[0]),
+                     "gpu_ne_cpu": int((s_gpu.cpu() != s_cpu).sum()),
+                     "cpu_eq_divide": bool(torch.equal(s_cpu, amax / 127)),
+                     "gpu_eq_times_reciprocal": bool(torch.equal(s_gpu.cpu(), recip)),
+                     "quantised_values_ne": int((i_gpu.cpu() != i_cpu).sum())}
+    return out
 
 
 _ORIG = {}

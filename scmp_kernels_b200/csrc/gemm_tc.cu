@@ -1105,6 +1105,7 @@ static bool env_on(const char* name) {
 struct Variant {
   bool pair, atmem, wide;  // wide without atmem: 512-wide tiles, a in shared memory
   bool f4;                 // e2m1 operands (kind::mxf4)
+  bool long_tiles;         // one accumulation unit of at least kShortTileStages stages
 };
 // f4_table: the call carries the e2m1-sliced stream table. e2m1 operands are
 // used on SM pairs with a in shared memory for streams of 64 to 512
@@ -1117,8 +1118,11 @@ static Variant choose_variant(int d, int unit_d, int lp, bool f4_table) {
   const int tlen = lp < 256 ? lp : 256;
   const int stages = (tlen < 256 ? cdiv(d, 256 / tlen) : d) * (lp / tlen);
   const bool long_tiles = v.pair && nunits == 1 && stages >= kShortTileStages;
+  v.long_tiles = long_tiles;
   v.atmem = long_tiles && env_on("SCMP_TC_ATMEM");
-  v.wide = long_tiles && (!v.atmem || lp < 256);  // wide_tiles<TLEN>() with atmem
+  // SCMP_TC_NARROW=1: long tiles on the two-accumulator kernel (tiles of at
+  // most 240 / 256 b rows, a tile's epilogue under the next tile's MMAs)
+  v.wide = long_tiles && (!v.atmem || lp < 256) && !(env_on("SCMP_TC_NARROW") && !v.atmem);
   v.f4 = f4_table && v.pair && !v.atmem && lp >= 64 && lp <= 512 && !env_on("SCMP_TC_INT8");
   return v;
 }
@@ -1226,7 +1230,7 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
         default: return launch_t<512, 1, true, false, true, true>(g, s, sms, st);
       }
     }
-    if (s.nunits > 1) {  // chunked path: stages unrolled
+    if (s.nunits > 1 || v.long_tiles) {  // chunked path and narrow long tiles: stages unrolled
       switch (g.lp) {
         case 64: return launch_t<64, 1, true, false, false, true, true>(g, s, sms, st);
         case 128: return launch_t<128, 1, true, false, false, true, true>(g, s, sms, st);

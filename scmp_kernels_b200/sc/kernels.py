@@ -341,6 +341,35 @@ def _launch(gran: int, mode: str, a: torch.Tensor, b: torch.Tensor, sc_prec: int
     return out
 
 
+def enable_matmul(tables: EnableTables, boundary_a: torch.Tensor, boundary_b: torch.Tensor,
+                  sign_a: Optional[torch.Tensor], sign_b: Optional[torch.Tensor], N: int, M: int, D: int,
+                  stoc_len: int, q_max_sq: float, is_bipolar: bool, flags: int = 0) -> torch.Tensor:
+    """Enable-signal matmul on already-quantised operands (the counterpart of
+    enable_matmul_triton, kernels.py:798-868, with this package's tables in
+    place of cum_indicator / k_table): boundary (N, D) / (M, D) int16, sign
+    int8 (bipolar only); returns (N, M) float32 fl32(S * fl32(q_max_sq / L))."""
+    if stoc_len != tables.L:
+        raise ValueError(f"enable_matmul: tables are for stoc_len={tables.L}, got {stoc_len}")
+    dev = boundary_a.device
+    ba = boundary_a.to(torch.int16).contiguous()
+    bb = boundary_b.to(torch.int16).contiguous()
+    sa = sign_a.to(torch.int8).contiguous() if is_bipolar else None
+    sb = sign_b.to(torch.int8).contiguous() if is_bipolar else None
+    amap, bmap = tables.maps_for(D)
+    out = torch.empty((N, M), dtype=torch.float32, device=dev)
+    L = _lib.lib()
+    ws_bytes = ctypes.c_size_t(0)
+    _lib.check(L.scmp_enable_matmul_workspace_size(N, M, D, ctypes.byref(ws_bytes)), "enable_matmul")
+    ws = torch.empty(max(ws_bytes.value, 1), dtype=torch.uint8, device=dev)
+    _lib.check(L.scmp_enable_matmul(
+        tables.ktab.data_ptr(), tables.pattern.data_ptr(), amap.data_ptr(), bmap.data_ptr(), tables.vcap,
+        tables.L, tables.lp, ba.data_ptr(), bb.data_ptr(), sa.data_ptr() if sa is not None else None,
+        sb.data_ptr() if sb is not None else None, N, M, D, float(q_max_sq), 1 if is_bipolar else 0,
+        out.data_ptr(), ws.data_ptr(), ws_bytes.value, flags | (_lib.FLAG_FORCE_SIMT if _FORCE_SIMT else 0),
+        ctypes.c_void_p(_lib.stream_handle(dev))), "enable_matmul")
+    return out
+
+
 def _prep_smooth(a, b, smooth_scales):
     """Fuse a / s and b * s into the device quantiser for float32 operands;
     other dtypes are smoothed in their own precision first, as the reference

@@ -331,6 +331,45 @@ def case_edges(names):
         _run("e_smooth_head", a, b, dict(granularity="per_head", mode="bipolar", sc_prec=8), smooth=s)
 
 
+def case_configs(names):
+    """The Sobol config builders of config_helpers.py:610-763 (antithetic,
+    alternative K seed, custom seeds with scrambles, DSE random seeds). The
+    reference's make_sobol_dse_config cannot be imported (its ``from rng import
+    Sobol`` fails), so that fixture's config comes from this package's builder
+    under a fixed ``random`` seed; the reference's sc_matmul consumes it."""
+    import random
+    from scmp_kernels.sc.config_helpers import (
+        make_sobol_altseed_config, make_sobol_antithetic_config, make_sobol_custom_seed_config)
+    from scmp_kernels_b200.sc.config_helpers import make_sobol_dse_config
+
+    def rnd(*shape, seed):
+        return torch.randn(*shape, generator=torch.Generator().manual_seed(seed))
+
+    C = {}
+    C["e_cfg_antithetic"] = (rnd(6, 40, seed=201), rnd(7, 40, seed=202),
+                             dict(granularity="per_row", mode="bipolar", sc_prec=8,
+                                  config=make_sobol_antithetic_config(40, 40, 8)))
+    C["e_cfg_altseed8"] = (rnd(6, 40, seed=203), rnd(7, 40, seed=204),
+                           dict(granularity="per_row", mode="bipolar", sc_prec=8,
+                                config=make_sobol_altseed_config(40, 40, 8)))
+    C["e_cfg_altseed6_prefix"] = (rnd(6, 36, seed=205), rnd(7, 36, seed=206),
+                                  dict(granularity="per_row", mode="unipolar", sc_prec=6, stoc_len=40,
+                                       config=make_sobol_altseed_config(36, 36, 6)))
+    random.seed(77)
+    C["e_cfg_custom_seed"] = (rnd(5, 32, seed=207), rnd(6, 32, seed=208),
+                              dict(granularity="per_row", mode="bipolar", sc_prec=8,
+                                   config=make_sobol_custom_seed_config(
+                                       32, 32, 8, q_seed=[1, 1, 3, 5, 15, 17, 51, 85],
+                                       k_seed=[1, 3, 7, 1, 9, 33, 41, 255], use_scrambling=True)))
+    random.seed(2024)
+    C["e_cfg_dse"] = (rnd(5, 32, seed=209), rnd(6, 32, seed=210),
+                      dict(granularity="per_tensor", mode="bipolar", sc_prec=8,
+                           config=make_sobol_dse_config(32, 32, 8)))
+    for nm, (a, b, p) in C.items():
+        if nm in names:
+            _run(nm, a, b, p)
+
+
 def case_rng(names):
     """RNG sequences, prepared prefixes and tables from the reference's own functions."""
     from scmp_kernels.sc.rng import Sobol, LFSR
@@ -369,6 +408,7 @@ def case_rng(names):
 ALL = {
     "rng": case_rng, "edges": case_edges,
     "cfg1": case_cfg1, "cfg3": case_cfg3, "cfg4": case_cfg4, "cfg5": case_cfg5, "cfg2": case_cfg2,
+    "configs": case_configs,
 }
 CASE_NAMES = {
     "rng": ["rng_golden"],
@@ -376,6 +416,7 @@ CASE_NAMES = {
     "cfg2": ["cfg2_slice"], "cfg3": ["cfg3_qk", "cfg3_av"],
     "cfg4": ["cfg4_L256", "cfg4_L128", "cfg4_L64", "cfg4_L128_grid256"],
     "cfg5": ["cfg5_slice"],
+    "configs": ["e_cfg_antithetic", "e_cfg_altseed8", "e_cfg_altseed6_prefix", "e_cfg_custom_seed", "e_cfg_dse"],
     "edges": ["e_rowgroup_bip", "e_rowgroup_uni", "e_row_uni_pertensor", "e_row3d_bip", "e_row3d_bip_gt",
               "e_row3d_uni", "e_tensor_uni_small", "e_halve", "e_prefix64", "e_rescale64", "e_rescale_long",
               "e_p4", "e_p6_uni_prefix", "e_chunk_rem", "e_chunk_ge_d", "e_chunk_short", "e_zeros",

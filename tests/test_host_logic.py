@@ -126,3 +126,23 @@ def test_config_builders_seeded_like_reference():
     import json
     z = np.load(os.path.join(GOLDEN, "e_lfsr_perelem.npz"))
     assert json.loads(str(z["params"]))["config"] == cfg
+
+
+@pytest.mark.parametrize("name,build", [
+    ("e_cfg_antithetic", lambda: C.make_sobol_antithetic_config(40, 40, 8)),
+    ("e_cfg_altseed8", lambda: C.make_sobol_altseed_config(40, 40, 8)),
+    ("e_cfg_altseed6_prefix", lambda: C.make_sobol_altseed_config(36, 36, 6)),
+    ("e_cfg_custom_seed", lambda: (random.seed(77), C.make_sobol_custom_seed_config(
+        32, 32, 8, q_seed=[1, 1, 3, 5, 15, 17, 51, 85], k_seed=[1, 3, 7, 1, 9, 33, 41, 255],
+        use_scrambling=True))[1]),
+    ("e_cfg_dse", lambda: (random.seed(2024), C.make_sobol_dse_config(32, 32, 8))[1]),
+])
+def test_sobol_config_builders_match_fixture_configs(name, build):
+    """The Sobol builders (config_helpers.py:610-763) give the configs the
+    fixtures were generated with: the reference's own builders for the
+    antithetic, alternative-seed and custom-seed variants (same draws from
+    Python's ``random`` for the scrambles), this package's for DSE, whose
+    reference builder cannot be imported."""
+    import json
+    z = np.load(os.path.join(GOLDEN, name + ".npz"))
+    assert json.loads(str(z["params"]))["config"] == build()
