@@ -211,7 +211,10 @@ def next_pow2(x: int) -> int:
 def k_table(ra: np.ndarray, L: int, V: int) -> np.ndarray:
     """``k_table[d, v] = #{t < L : ra[d, t] < v}`` (kernels.py:140-169)."""
     v = np.arange(V)
-    return (ra[:, :L, None] < v[None, None, :]).sum(axis=1).astype(np.int32)
+    # computed once per distinct sequence row (large D repeats few rows)
+    rows, inv = np.unique(np.asarray(ra)[:, :L], axis=0, return_inverse=True)
+    kt = (rows[:, :, None] < v[None, None, :]).sum(axis=1).astype(np.int32)
+    return kt[np.asarray(inv).reshape(-1)]
 
 
 def count_table(rb_row: np.ndarray, L: int, V: int) -> np.ndarray:

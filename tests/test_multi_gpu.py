@@ -90,3 +90,35 @@ def test_sharded_fused_and_gathered_equal_single_gpu():
     for rank, status, val in out:
         assert status == "ok", val
         assert all(val.values()), f"rank {rank}: {val}"
+
+
+@pytest.mark.parametrize("granularity,chunk_d,shape", [
+    ("per_tensor", 0, "2d"),
+    ("per_row", 0, "2d"),
+    ("per_row", 128, "2d"),
+    ("per_row", 0, "3d"),
+    ("per_head", 0, "3d"),
+    ("per_row", 0, "2d_long"),
+])
+def test_runs_on_second_gpu(granularity, chunk_d, shape):
+    """One process, two devices (the reference's multi-GPU device guard,
+    tests/test_sc_smoke.py:139-172): inputs on cuda:1 with cuda:0 current run
+    on cuda:1, leave cuda:0 current and equal the cuda:0 result. The "2d_long"
+    case launches the wide-tile GEMM (over 48 KB of shared memory, a per-device
+    kernel attribute) on cuda:0, then cuda:1, then cuda:0 again."""
+    sys.path.insert(0, REPO)
+    from scmp_kernels_b200 import sc_matmul
+    torch.manual_seed(0)
+    if shape == "2d":
+        a0, b0 = torch.randn(8, 256, device="cuda:0"), torch.randn(16, 256, device="cuda:0")
+    elif shape == "2d_long":
+        a0, b0 = torch.randn(300, 1000, device="cuda:0"), torch.randn(520, 1000, device="cuda:0")
+    else:
+        a0, b0 = torch.randn(4, 8, 64, device="cuda:0"), torch.randn(4, 16, 64, device="cuda:0")
+    torch.cuda.set_device(0)
+    y0 = sc_matmul(a0, b0, granularity=granularity, chunk_d=chunk_d, sc_prec=8)
+    y1 = sc_matmul(a0.to("cuda:1"), b0.to("cuda:1"), granularity=granularity, chunk_d=chunk_d, sc_prec=8)
+    y2 = sc_matmul(a0, b0, granularity=granularity, chunk_d=chunk_d, sc_prec=8)
+    assert y1.device.index == 1
+    assert torch.cuda.current_device() == 0
+    assert torch.equal(y0.cpu(), y1.cpu()) and torch.equal(y0, y2)
