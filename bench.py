@@ -291,7 +291,7 @@ def run_reference(args, rank, world):
 def measure(name, shape, args, rank, world, dev, sampler=None, check_rows=128):
     import torch
     import torch.distributed as dist
-    from scmp_kernels_b200 import _lib, sc_matmul
+    from scmp_kernels_b200 import _lib, sc_matmul, sc_matmul_levels
     from scmp_kernels_b200 import dist as SD
 
     a, b_full, s, kw, (BH, N, M, D), L = build_workload(name, dev, shape)
@@ -303,17 +303,24 @@ def measure(name, shape, args, rank, world, dev, sampler=None, check_rows=128):
     kw = dict(kw)
     if s is not None:
         kw["smooth_scales"] = s
-    calls = [(None, kw)]
     if name == "config4":
+        # the caller's mixed precision: row groups of 4 by range tercile, one
+        # call with a stream length per row (sc_matmul_levels)
         from scmp_kernels_b200 import workloads as W
-        lv = W.mp_row_levels(a, 4, (256, 128, 64))
-        calls = [(rows_.to(dev), dict(kw, stoc_len=Lv, rng_levels=Lv)) for Lv, rows_ in lv.items()]
+        rl, Ls = W.mp_row_level_index(a, 4, (256, 128, 64))
+        kw = dict(kw, row_levels=rl, stoc_len_levels=Ls, rng_levels="stoc_len")
+    calls = [(None, kw)]
     a_parts = [a if idx is None else a[idx].contiguous() for idx, _ in calls]
+
+    def mm(ai, b_, ci):
+        if "row_levels" in ci:
+            return sc_matmul_levels(ai, b_, **ci)
+        return sc_matmul(ai, b_, **ci)
 
     def one_call(ai, b_, ci):
         if world > 1:  # this rank's column block, stored into every rank's output
             return SD.sc_matmul_sharded(ai, b_, M, copy=False, **ci)
-        return sc_matmul(ai, b_, **ci)
+        return mm(ai, b_, ci)
 
     def assemble(ys):
         if len(ys) == 1:
@@ -383,7 +390,8 @@ def measure(name, shape, args, rank, world, dev, sampler=None, check_rows=128):
         rows = sorted(set(range(min(check_rows, N))) | set(range(max(0, N - check_rows), N)))
         idx = torch.tensor(rows, device=dev)
         ok_t = torch.ones(1, device=dev)
-        ref = sc_matmul(a[idx].contiguous(), b_full, **kw)
+        kw_rows = dict(kw, row_levels=kw["row_levels"][idx]) if "row_levels" in kw else kw
+        ref = mm(a[idx].contiguous(), b_full, kw_rows)
         if not torch.equal(y[idx], ref):
             ok_t.zero_()
         dist.all_reduce(ok_t, op=dist.ReduceOp.MIN)
@@ -403,12 +411,14 @@ def measure(name, shape, args, rank, world, dev, sampler=None, check_rows=128):
             ci_host = dict(calls[0][1])
             if hs is not None:
                 ci_host["smooth_scales"] = hs
+            if "row_levels" in ci_host:  # the row levels come from the host too
+                ci_host["row_levels"] = ci_host["row_levels"].cpu().pin_memory()
             if world > 1:
                 def e2e_step():  # this rank's column block back to host memory, no gather
                     return SD.sc_matmul_sharded(ha[0], hb, M, gather=False, **ci_host)
             else:
                 def e2e_step():  # streamed host path; result in pinned host memory
-                    return sc_matmul(ha[0], hb, **ci_host)
+                    return mm(ha[0], hb, ci_host)
         else:
             hy = torch.empty(a.shape[:-1] + ((hi - lo) if world > 1 else M,), dtype=torch.float32).pin_memory()
 
@@ -434,6 +444,8 @@ def measure(name, shape, args, rank, world, dev, sampler=None, check_rows=128):
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             e_ms = tt.item()
         bi = sum(x.numel() * 4 for x in ha) + hb.numel() * 4 + (hs.numel() * 4 if hs is not None else 0)
+        if len(calls) == 1 and "row_levels" in ci_host:
+            bi += ci_host["row_levels"].numel() * 4
         res["e2e"] = {"value": ops / (e_ms * 1e-3) / 1e9, "unit": "GOPS", "h2d_bytes_per_step": bi,
                       "d2h_bytes_per_step": out_bytes, "ms_per_step": e_ms,
                       "output": ("each rank's column block of the result to its host memory (the result "

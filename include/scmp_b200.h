@@ -175,6 +175,44 @@ int scmp_sc_matmul(const scmp_matmul_desc* desc, void* workspace, size_t workspa
                    void* stream);
 
 /*
+ * Row levels: rows of a in groups with their own stream lengths, in one call
+ * (one quantisation pass over a, one SC-GEMM launch).
+ *
+ * Replaces the caller-side mixed precision of the reference: rows classified
+ * into levels (classify_rows_by_metric, scmp_kernels/mp/config.py:154-191,
+ * and the range classifier of :924-1007) and one sc_matmul per level on the
+ * gathered rows, scattered back (the per-level calls of the chunked MLP path,
+ * sc/kernels.py:1443-1566). The result equals that composition bit for bit:
+ * row i of a is computed with the stream length, grid and tables of level
+ * row_level[i].
+ *
+ * desc: as for scmp_sc_matmul with granularity SCMP_PER_ROW, batch 1 and
+ * either chunk_d > 0 (bipolar, chunked path; group sizes are ignored there,
+ * as in the reference) or group_a == 1; its stoc_len, rng_levels, ktab,
+ * pattern, pattern4, amap, bmap, vcap and lp are not used (the levels carry
+ * them) and neither is SCMP_FLAG_B_READY. levels: n_levels (1..4) HOST
+ * descriptors with each level's tables from scmp_build_tables (pattern4
+ * required; padded stream lengths 64..512). row_level: DEVICE int32 (n,),
+ * the level of every row of a; a row with a level outside [0, n_levels) is
+ * left out of the result and recorded as a device error. Runs on SM pairs of
+ * an sm_100 device only (SCMP_ERR_UNSUPPORTED otherwise).
+ */
+typedef struct scmp_level_desc {
+  int stoc_len;             /* L of this level                                  */
+  int rng_levels;           /* G of this level                                  */
+  int vcap, lp;             /* as passed to scmp_build_tables for this level    */
+  const int16_t* ktab;      /* this level's tables (scmp_build_tables)          */
+  const uint32_t* pattern4;
+  const int32_t* amap;      /* (d,) table row of every dimension, as for scmp_matmul_desc */
+  const int32_t* bmap;
+} scmp_level_desc;
+
+int scmp_sc_matmul_levels_workspace_size(const scmp_matmul_desc* desc, const scmp_level_desc* levels,
+                                         int n_levels, size_t* bytes);
+int scmp_sc_matmul_levels(const scmp_matmul_desc* desc, const scmp_level_desc* levels, int n_levels,
+                          const int32_t* row_level, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * scmp_sc_matmul without a caller workspace. No counterpart in the reference.
  * For callers that cannot allocate device memory (a host reaching this
  * library through a plain C FFI with no device allocator, or a process that

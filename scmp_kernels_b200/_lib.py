@@ -48,6 +48,16 @@ class MatmulDesc(ctypes.Structure):
     ]
 
 
+class LevelDesc(ctypes.Structure):
+    """Mirror of ``scmp_level_desc``."""
+    _fields_ = [
+        ("stoc_len", c_int), ("rng_levels", c_int), ("vcap", c_int), ("lp", c_int),
+        ("ktab", c_void_p), ("pattern4", c_void_p), ("amap", c_void_p), ("bmap", c_void_p),
+    ]
+
+
+MAX_LEVELS = 4
+
 # name -> (restype, argtypes); every symbol of include/scmp_b200.h
 SIGNATURES = {
     "scmp_abi_version": (c_int, []),
@@ -65,6 +75,10 @@ SIGNATURES = {
     "scmp_sc_matmul_workspace_size": (c_int, [ctypes.POINTER(MatmulDesc), ctypes.POINTER(c_size_t)]),
     "scmp_sc_matmul": (c_int, [ctypes.POINTER(MatmulDesc), c_void_p, c_size_t, c_void_p]),
     "scmp_sc_matmul_noalloc": (c_int, [ctypes.POINTER(MatmulDesc), c_void_p]),
+    "scmp_sc_matmul_levels_workspace_size": (c_int, [ctypes.POINTER(MatmulDesc), ctypes.POINTER(LevelDesc), c_int,
+                                                     ctypes.POINTER(c_size_t)]),
+    "scmp_sc_matmul_levels": (c_int, [ctypes.POINTER(MatmulDesc), ctypes.POINTER(LevelDesc), c_int, c_void_p,
+                                      c_void_p, c_size_t, c_void_p]),
     "scmp_enable_matmul_workspace_size": (c_int, [c_int, c_int, c_int, ctypes.POINTER(c_size_t)]),
     "scmp_enable_matmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                    c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,

@@ -295,8 +295,11 @@ __device__ __forceinline__ void store_rows32(const GemmArgs& g, uint32_t stg, in
     const int r = 4 * rr + (lane >> 3);
     const uint4 x = ld_shared_v4(stg + r * 128 + ((c ^ (r & 7)) << 4));
     const int ia = ia0 + r;
-    if (ia < g.n && ib < m_end) {
-      const long long idx = g.out_off + ((long long)bh * g.n + ia) * g.out_ld + ib;
+    // result row (with row levels, the permuted row's place in the result)
+    int orow = ia < g.n ? ia : -1;
+    if (g.row_of && orow >= 0) orow = __ldg(g.row_of + ia);
+    if (orow >= 0 && ib < m_end) {
+      const long long idx = g.out_off + ((long long)bh * (g.row_of ? g.n_out : g.n) + orow) * g.out_ld + ib;
       const bool whole = g.out_vec && ib + 3 < m_end;
 #pragma unroll 1
       for (int k = 0; k < g.nouts; ++k) {
@@ -330,6 +333,7 @@ struct Sched {
   int tail_w;   // workers sharing the tail tiles' K range (0: no tail)
   int tail_blk; // blocks of eight dimensions in the tail: (tiles - full) * nblk
   int nwork, nblk;
+  int band_group;  // bands of a per group of the tile order (tile_coords)
 };
 
 // Work items of a worker: whole tiles w = worker, worker + workers, ... < full,
@@ -392,12 +396,19 @@ __device__ __forceinline__ void unit_range(const Sched& s, const Work& k, int u,
   }
 }
 
+// Tile order: bands of a (tile_a rows) in groups of `band_group`; inside a
+// group, b's tiles one after another, each for every band of the group, so
+// that the tiles running at the same time share b's operand rows and the
+// group's a rows in L2.
 __device__ __forceinline__ void tile_coords(const Sched& s, int tile, int& bh, int& a0, int& b0) {
   const int per = s.tiles_a * s.tiles_b;
   bh = tile / per;
   const int r = tile % per;
-  a0 = (r / s.tiles_b) * s.tile_a;
-  b0 = (r % s.tiles_b) * s.tile_b;
+  const int G = s.band_group;
+  const int grp = r / (G * s.tiles_b), j = r % (G * s.tiles_b);
+  const int gb = min(G, s.tiles_a - grp * G);  // bands in this group (the last may have fewer)
+  a0 = (grp * G + j % gb) * s.tile_a;
+  b0 = (j / gb) * s.tile_b;
 }
 
 template <int TLEN, int SPD, bool F4 = false>
@@ -424,7 +435,7 @@ __device__ __forceinline__ int bm_at(const int4& lo, const int4& hi, int e) {
 // is the same for every lane of the warp (config 5: 2% faster; with longer
 // streams, 32-byte loads, skipping them is 1% faster).
 template <int TLEN, int SPD, bool F4 = false>
-__device__ __forceinline__ void load_stream_words(const GemmArgs& g, const uint32_t* __restrict__ pat,
+__device__ __forceinline__ void load_stream_words(int vcap1, const uint32_t* __restrict__ pat,
                                                   const uint4& kv, const int4& bl, const int4& bh, int j,
                                                   int dbase, int d1, bool valid, uint32_t LW,
                                                   uint32_t (&pw)[F4 ? 16 : 8]) {
@@ -437,7 +448,7 @@ __device__ __forceinline__ void load_stream_words(const GemmArgs& g, const uint3
     const int v = kv_at(kv, e);
     const int mag = v < 0 ? -v : v;
     if (TLEN <= 64 ? dbase + e < d1 : (valid && dbase + e < d1 && mag != 0)) {
-      const uint32_t* p = pat + ((size_t)bm_at(bl, bh, e) * (g.vcap + 1) + mag) * LW + (j % SPD) * NW;
+      const uint32_t* p = pat + ((size_t)bm_at(bl, bh, e) * vcap1 + mag) * LW + (j % SPD) * NW;
       if constexpr (NW >= 4) {
 #pragma unroll
         for (int x = 0; x < NW / 4; ++x) {
@@ -478,10 +489,38 @@ __device__ __forceinline__ int stages_of_unit(int len) {
 // memory at tmem_a (this thread's lane, first stage column) instead.
 // With F4 the words are e2m1: eight 4-bit values (0, +1 = 0x2, -1 = 0xA) per
 // 32-bit word, so a 16-byte chunk covers 32 positions instead of 16.
+// b's side of one work item: its quantised operand, stream table and row map
+// (one set per call, or the level's with row levels).
+struct BSide {
+  const uint32_t* pat;
+  const uint4* kv;
+  const int4* bm;
+  uint32_t LW;
+  int vcap1;
+};
+
+// Level of the a tile starting at permuted row a0, -1 for a tile past the
+// last level (row levels only).
+__device__ __forceinline__ int level_of(const GemmArgs& g, int a0) {
+  const int t = a0 >> 8;
+  for (int l = 0; l < g.nlev; ++l)
+    if (t < __ldg(g.lev_tile0 + l + 1)) return l;
+  return -1;
+}
+
+// Stages of an accumulation unit of `len` dimensions for padded stream
+// length lp (runtime form of stages_of_unit for the row-level kernel).
+__device__ __forceinline__ int stages_rt(int lp, bool f4, int len) {
+  const int sp = f4 ? 512 : 256;
+  return lp < sp ? cdiv(len, sp / lp) : len * (lp / sp);
+}
+
+// The stages of one work item (all its accumulation units).
 template <bool SIDE_A, int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE, bool F4, bool UNR>
-__device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint32_t sbase, uint32_t bar_base,
-                                        volatile int* abort_flag, uint32_t rank, int tile0, int tstep, int r,
-                                        int lane, uint32_t tmem_a) {
+__device__ __forceinline__ bool produce_item(const GemmArgs& g, const Sched& sc, const Work& wk, const BSide& bs,
+                                             uint32_t sbase, uint32_t bar_base, volatile int* abort_flag,
+                                             uint32_t rank, int r, int lane, uint32_t tmem_a,
+                                             const uint32_t (&xo)[8], uint32_t& it) {
   using C = Cfg<PAIR, ATMEM, WIDE, F4>;
   constexpr int NST = C::NST;
   constexpr int DPS = dims_per_stage<TLEN, F4>();
@@ -489,18 +528,11 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
   constexpr int NPW = F4 ? 16 : 8;  // stream words per stage
   // 16-byte chunks of one dimension in a stage
   constexpr int CPDS = (TLEN < stage_positions<F4>() ? TLEN : stage_positions<F4>()) / (F4 ? 32 : 16);
-  const uint32_t* __restrict__ pat = F4 ? g.pattern4 : g.pattern;
   const int R = SIDE_A ? g.batch * g.n : g.batch * g.m;
-  const uint4* kvsrc = reinterpret_cast<const uint4*>(SIDE_A ? g.ka : g.vb);
-  const int4* bmsrc = reinterpret_cast<const int4*>(g.bmap);
-  const uint32_t LW = (uint32_t)g.lp / 32;
-  // byte offset of 16-byte chunk k (0..7) of row r in a 128-byte-swizzled atom
-  uint32_t xo[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) xo[k] = (uint32_t)r * 128u + (uint32_t)((k ^ (r & 7)) << 4);
-  uint32_t it = 0;
-  for (int w = tile0; w < sc.nwork; w += tstep) {
-    const Work wk = work_of(sc, w, g.d);
+  const uint4* kvsrc = SIDE_A ? reinterpret_cast<const uint4*>(g.ka) : bs.kv;
+  const int4* bmsrc = bs.bm;
+  const uint32_t LW = bs.LW;
+  {
     int bh, a0, b0;
     tile_coords(sc, wk.tile, bh, a0, b0);
     // b: the tile's tile_b rows, tile_b / NCTA per CTA (rows past them are not
@@ -530,7 +562,7 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
       if (!SIDE_A) {
         bm_lo = __ldg(bmsrc + 2 * blk0);
         bm_hi = __ldg(bmsrc + 2 * blk0 + 1);
-        load_stream_words<TLEN, SPD, F4>(g, pat, kv_cur, bm_lo, bm_hi, 0, d0, d1, valid, LW, pw);
+        load_stream_words<TLEN, SPD, F4>(bs.vcap1, bs.pat, kv_cur, bm_lo, bm_hi, 0, d0, d1, valid, LW, pw);
       }
       for (int blk = 0; blk < nblk; ++blk) {
         const int dbase = d0 + 8 * blk;
@@ -558,9 +590,9 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
           uint32_t pn[NPW];
           if (!SIDE_A) {
             if (j + 1 < NSPB)
-              load_stream_words<TLEN, SPD, F4>(g, pat, kv_cur, bm_lo, bm_hi, j + 1, dbase, d1, valid, LW, pn);
+              load_stream_words<TLEN, SPD, F4>(bs.vcap1, bs.pat, kv_cur, bm_lo, bm_hi, j + 1, dbase, d1, valid, LW, pn);
             else
-              load_stream_words<TLEN, SPD, F4>(g, pat, kv_nxt, nb_lo, nb_hi, 0, dbase + 8, more ? d1 : dbase, valid,
+              load_stream_words<TLEN, SPD, F4>(bs.vcap1, bs.pat, kv_nxt, nb_lo, nb_hi, 0, dbase + 8, more ? d1 : dbase, valid,
                                                LW, pn);
           }
           const int s = it % NST;
@@ -670,10 +702,65 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
   return true;
 }
 
+// Producer loop of one operand side over the worker's items. LEV (row
+// levels): each item's stream length is its level's, dispatched at run time.
+template <bool SIDE_A, int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE, bool F4, bool UNR, bool LEV>
+__device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint32_t sbase, uint32_t bar_base,
+                                        volatile int* abort_flag, uint32_t rank, int tile0, int tstep, int r,
+                                        int lane, uint32_t tmem_a) {
+  // byte offset of 16-byte chunk k (0..7) of row r in a 128-byte-swizzled atom
+  uint32_t xo[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) xo[k] = (uint32_t)r * 128u + (uint32_t)((k ^ (r & 7)) << 4);
+  uint32_t it = 0;
+  for (int w = tile0; w < sc.nwork; w += tstep) {
+    const Work wk = work_of(sc, w, g.d);
+    if constexpr (LEV) {
+      int bh, a0, b0;
+      tile_coords(sc, wk.tile, bh, a0, b0);
+      const int lv = level_of(g, a0);
+      if (lv < 0) continue;
+      const LevelB& L = g.lev[lv];
+      const BSide bs{L.pattern4, reinterpret_cast<const uint4*>(L.vb), reinterpret_cast<const int4*>(L.bmap),
+                     (uint32_t)L.lp / 32, L.vcap + 1};
+      bool ok;
+      switch (L.lp) {
+        case 64:
+          ok = produce_item<SIDE_A, 64, 1, PAIR, ATMEM, WIDE, F4, UNR>(g, sc, wk, bs, sbase, bar_base, abort_flag,
+                                                                      rank, r, lane, tmem_a, xo, it);
+          break;
+        case 128:
+          ok = produce_item<SIDE_A, 128, 1, PAIR, ATMEM, WIDE, F4, UNR>(g, sc, wk, bs, sbase, bar_base, abort_flag,
+                                                                       rank, r, lane, tmem_a, xo, it);
+          break;
+        case 256:
+          ok = produce_item<SIDE_A, 256, 1, PAIR, ATMEM, WIDE, F4, UNR>(g, sc, wk, bs, sbase, bar_base, abort_flag,
+                                                                       rank, r, lane, tmem_a, xo, it);
+          break;
+        default:
+          ok = produce_item<SIDE_A, 512, 1, PAIR, ATMEM, WIDE, F4, UNR>(g, sc, wk, bs, sbase, bar_base, abort_flag,
+                                                                       rank, r, lane, tmem_a, xo, it);
+          break;
+      }
+      if (!ok) return false;
+    } else {
+      const BSide bs{F4 ? g.pattern4 : g.pattern, reinterpret_cast<const uint4*>(g.vb),
+                     reinterpret_cast<const int4*>(g.bmap), (uint32_t)g.lp / 32, g.vcap + 1};
+      if (!produce_item<SIDE_A, TLEN, SPD, PAIR, ATMEM, WIDE, F4, UNR>(g, sc, wk, bs, sbase, bar_base, abort_flag,
+                                                                      rank, r, lane, tmem_a, xo, it))
+        return false;
+    }
+  }
+  return true;
+}
+
 
 // TLEN: padded stream length lp when lp <= 256 (256/lp dimensions per stage),
 // or 256 when lp = 256*SPD (SPD stages per dimension, SPD = 1 or 2).
-template <int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE, bool F4, bool UNR>
+// LEV: row levels (GemmArgs.nlev > 0): every a tile belongs to one level,
+// whose stream length (TLEN is then unused), b operand, tables and epilogue
+// scale the item uses; tiles past the last level are skipped by every role.
+template <int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE, bool F4, bool UNR, bool LEV = false>
 __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched sc) {
   using C = Cfg<PAIR, ATMEM, WIDE, F4>;
   constexpr int NST = C::NST;
@@ -752,7 +839,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
 
   // MMAs of accumulation unit u of work item wk into accumulator buffer uc % nbuf
   // (leader CTA, one thread); it counts the K stages consumed. False on abort.
-  auto issue_unit = [&](const Work& wk, int u, uint32_t& it, uint32_t uc) -> bool {
+  auto issue_unit = [&](const Work& wk, int u, uint32_t& it, uint32_t uc, int lp) -> bool {
     const int nmma = C::WIDE ? 2 : 1;  // MMAs per K step
     const int nw = sc.tile_b / nmma;   // width of each
     const uint32_t idesc = C::idesc_n(nw);
@@ -762,7 +849,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
     tc_fence_after();
     int d0, d1;
     unit_range(sc, wk, u, g.d, d0, d1);
-    const int nst = stages_of_unit<TLEN, F4>(d1 - d0) * SPD;
+    const int nst = LEV ? stages_rt(lp, F4, d1 - d0) : stages_of_unit<TLEN, F4>(d1 - d0) * SPD;
     for (int st = 0; st < nst; ++st, ++it) {
       const int s = it % NST;
       if (!mbar_wait(full_bar(s), (it / NST) & 1, abort_flag, 3)) return false;
@@ -812,10 +899,10 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
     // ------------------------------------------------------------ producers
     // a's warp w writes tensor-memory lanes 32w..32w+31 (its rows)
     if (warp < PROD_A_WARPS)
-      produce<true, TLEN, SPD, PAIR, ATMEM, WIDE, F4, UNR>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep, threadIdx.x,
+      produce<true, TLEN, SPD, PAIR, ATMEM, WIDE, F4, UNR, LEV>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep, threadIdx.x,
                                             lane, tmem + ((uint32_t)(32 * warp) << 16) + C::TMEM_A);
     else
-      produce<false, TLEN, SPD, PAIR, ATMEM, WIDE, F4, UNR>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep,
+      produce<false, TLEN, SPD, PAIR, ATMEM, WIDE, F4, UNR, LEV>(g, sc, sbase, bar_base, abort_flag, rank, tile0, tstep,
                                              threadIdx.x - PROD_A_WARPS * 32, lane, 0u);
   } else if (!C::MERGED && warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer (leader CTA)
@@ -823,9 +910,17 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
       uint32_t it = 0, uc = 0;
       for (int w = tile0; w < sc.nwork; w += tstep) {
         const Work wk = work_of(sc, w, g.d);
+        int lp = g.lp;
+        if constexpr (LEV) {
+          int bh, a0, b0;
+          tile_coords(sc, wk.tile, bh, a0, b0);
+          const int lv = level_of(g, a0);
+          if (lv < 0) continue;
+          lp = g.lev[lv].lp;
+        }
         const int nu = units_of(sc, wk);
         for (int u = 0; u < nu; ++u, ++uc)
-          if (!issue_unit(wk, u, it, uc)) goto mma_done;
+          if (!issue_unit(wk, u, it, uc, lp)) goto mma_done;
       }
     mma_done:
       drain();
@@ -843,13 +938,22 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
     for (int w = tile0; w < sc.nwork; w += tstep) {
       const Work wk = work_of(sc, w, g.d);
       if (units_of(sc, wk) == 0) continue;  // empty tail piece
-      if (issuer) {  // one accumulation unit per item with wide tiles
-        int ok = 1;
-        if (lane == 0) ok = issue_unit(wk, 0, mit, uc) ? 1 : 0;
-        if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) goto epi_out;
-      }
       int bh, a0, b0;
       tile_coords(sc, wk.tile, bh, a0, b0);
+      // the item's epilogue recipe (with row levels, its level's scale)
+      Epilogue ep = g.epi;
+      int lp = g.lp;
+      if constexpr (LEV) {
+        const int lv = level_of(g, a0);
+        if (lv < 0) continue;
+        ep.inner = g.lev[lv].inner;
+        lp = g.lev[lv].lp;
+      }
+      if (issuer) {  // one accumulation unit per item with wide tiles
+        int ok = 1;
+        if (lane == 0) ok = issue_unit(wk, 0, mit, uc, lp) ? 1 : 0;
+        if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) goto epi_out;
+      }
       const int ia = a0 + (int)rank * C::BM + 32 * q + lane;
       const int m_end = min(g.m, b0 + sc.tile_b);  // end of this tile's columns
       if (wk.part >= 0) {
@@ -915,7 +1019,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
                 const int ib = b0 + cb * 16 + j;
                 fin[16 * h + j] =
                     (ia < g.n && ib < m_end)
-                        ? __float_as_uint(epi_value(g.epi, (int)acc[j], bh * g.n + ia, bh * g.m + ib, bh, 0, g.n, g.m))
+                        ? __float_as_uint(epi_value(ep, (int)acc[j], bh * g.n + ia, bh * g.m + ib, bh, 0, g.n, g.m))
                         : 0u;
               }
             }
@@ -927,7 +1031,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
         if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar(buf), rank);
         continue;
       }
-      const bool chunked = g.epi.kind == EPI_CHUNK;
+      const bool chunked = ep.kind == EPI_CHUNK;
       for (int u = 0; u < sc.nunits; ++u, ++uc) {
         const int buf = (int)(uc % nbuf);
         if (!mbar_wait(accf_bar(buf), (uc / nbuf) & 1, abort_flag, 5)) goto epi_out;
@@ -941,9 +1045,9 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
           const int et = (warp - C::EPI_WARP0) * 32 + lane;
           asm volatile("bar.sync 1, 128;" ::: "memory");  // the previous chunk's readers are done
           for (int c = et; c < sc.tile_b; c += 128)
-            sbs[c] = b0 + c < g.m ? __ldg(g.epi.sb + (size_t)u * g.m + b0 + c) : 0.f;
+            sbs[c] = b0 + c < g.m ? __ldg(ep.sb + (size_t)u * g.m + b0 + c) : 0.f;
           asm volatile("bar.sync 1, 128;" ::: "memory");
-          const float sar = ia < g.n ? __ldg(g.epi.sa + (size_t)u * g.n + ia) : 0.f;
+          const float sar = ia < g.n ? __ldg(ep.sa + (size_t)u * g.n + ia) : 0.f;
           const int ns = cdiv(sc.tile_b, 8);  // slices of eight columns
           uint32_t acc0[8], run0[8], acc1[8], run1[8];
           // result of slice cb into acc (in place), stored to the running sum
@@ -953,7 +1057,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
               const int ib = b0 + cb * 8 + j;
               float x = 0.f;
               if (ia < g.n && ib < m_end)
-                x = fmul(fmul((float)acc_int<F4>(acc[j]), g.epi.inner), fmul(sar, sbs[cb * 8 + j]));
+                x = fmul(fmul((float)acc_int<F4>(acc[j]), ep.inner), fmul(sar, sbs[cb * 8 + j]));
               acc[j] = __float_as_uint(fadd(u > 0 ? __uint_as_float(run[j]) : 0.f, x));
             }
             TMEM_ST8(lane_addr + C::ACC_STRIDE + cb * 8, acc);
@@ -1000,7 +1104,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
               const int ib = b0 + cb * 16 + j;
               float v = 0.f;
               if (ia < g.n && ib < m_end)
-                v = epi_value(g.epi, acc_int<F4>(acc[j]), bh * g.n + ia, bh * g.m + ib, bh, u, g.n, g.m);
+                v = epi_value(ep, acc_int<F4>(acc[j]), bh * g.n + ia, bh * g.m + ib, bh, u, g.n, g.m);
               if (chunked) v = fadd(u > 0 ? __uint_as_float(run[j]) : 0.f, v);
               fin[16 * h + j] = __float_as_uint(v);
             }
@@ -1032,10 +1136,10 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
 }
 
 template <int TLEN, int SPD, bool PAIR, bool ATMEM = false, bool WIDE = ATMEM && wide_tiles<TLEN>(), bool F4 = false,
-          bool UNR = F4 && WIDE>
+          bool UNR = F4 && WIDE, bool LEV = false>
 static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int sms, cudaStream_t st) {
   using C = Cfg<PAIR, ATMEM, WIDE, F4>;
-  auto kern = gemm_tc_kernel<TLEN, SPD, PAIR, ATMEM, WIDE, F4, UNR>;
+  auto kern = gemm_tc_kernel<TLEN, SPD, PAIR, ATMEM, WIDE, F4, UNR, LEV>;
   // The attribute belongs to the current device's context, so it is set on
   // every launch (a host call; a process may drive several devices).
   {
@@ -1185,6 +1289,9 @@ static Sched make_sched(int batch, int n, int m, int d, int unit_d, Variant v, i
     }
   }
   s.nwork = s.full + (s.tail_w > 0 ? 2 * s.workers : 0);
+  const char* bg = getenv("SCMP_TC_BAND_GROUP");
+  s.band_group = bg ? atoi(bg) : 1;
+  if (s.band_group < 1) s.band_group = 1;
   return s;
 }
 }  // namespace tc
@@ -1280,6 +1387,44 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
     case 128: return launch_t<128, 1, false>(g, s, sms, st);
     default: return spd == 2 ? launch_t<256, 2, false>(g, s, sms, st) : launch_t<256, 1, false>(g, s, sms, st);
   }
+}
+
+// Row levels: one launch on SM pairs with e2m1 operands; every level's
+// padded stream length in [64, 512]. a's permuted rows (g.n, whole 256-row
+// tiles) bound the schedule; tiles past the last level's end are skipped.
+// Whole tiles only (the tail is not shared over K).
+bool gemm_tc_levels_supported(const GemmArgs& g) {
+  if (g.nlev < 1 || g.nlev > kMaxLevels || g.n % 256 != 0 || g.m <= 0 || g.d <= 0 || g.batch != 1) return false;
+  if (g.unit_d > 0 && g.unit_d < g.d && g.unit_d % 8 != 0) return false;
+  for (int l = 0; l < g.nlev; ++l) {
+    const int lp = g.lev[l].lp;
+    if (lp < 64 || lp > 512 || (lp & (lp - 1)) || !g.lev[l].pattern4) return false;
+    if ((long long)g.d * g.lev[l].L >= (1LL << 31)) return false;
+  }
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  return major == 10 && minor == 0;
+}
+
+cudaError_t launch_gemm_tc_levels(const GemmArgs& g, cudaStream_t st) {
+  using namespace tc;
+  const int sms = device_sms();
+  int min_lp = 512;
+  for (int l = 0; l < g.nlev; ++l) min_lp = g.lev[l].lp < min_lp ? g.lev[l].lp : min_lp;
+  // wide tiles when every level's tiles are long (one accumulation unit)
+  Variant v = choose_variant(g.d, g.unit_d, min_lp, true);
+  v.f4 = true;
+  v.pair = true;
+  v.atmem = false;
+  Sched s = make_sched(g.batch, g.n, g.m, g.d, g.unit_d, v, sms);
+  s.full = s.tiles;
+  s.tail_w = 0;
+  s.nwork = s.tiles;
+  s.workers = s.tiles < sms / 2 ? s.tiles : sms / 2;
+  if (v.wide) return launch_t<256, 1, true, false, true, true, true, true>(g, s, sms, st);
+  return launch_t<256, 1, true, false, false, true, true, true>(g, s, sms, st);
 }
 
 }  // namespace scmp

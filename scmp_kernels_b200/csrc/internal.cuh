@@ -108,6 +108,19 @@ __device__ __forceinline__ uint32_t unslice(uint32_t w) {
 //   chunks of the chunked path; one unit of d otherwise).
 constexpr int kMaxOuts = SCMP_MAX_OUT_PEERS;  // destinations of one result
 
+// Row groups of a with their own stream lengths in one GEMM (the caller's
+// mixed precision, scmp_kernels/mp/config.py:154-191): a's rows are permuted
+// so that every level occupies whole 256-row tiles, level l holding permuted
+// rows [256 * tile0[l], 256 * tile0[l + 1]); b is quantised once per level.
+constexpr int kMaxLevels = 4;
+struct LevelB {
+  const int16_t* vb;         // b's operand quantised on this level's grid (blocked layout)
+  const uint32_t* pattern4;  // this level's e2m1-sliced stream table
+  const int32_t* bmap;       // padded dimension -> table row map
+  int vcap, lp, L;
+  float inner;               // fl32(q_max^2 / L)
+};
+
 // Writes v to element (h, i, j) of every destination of the result.
 struct GemmArgs;
 __device__ __forceinline__ void store_out(const GemmArgs& g, int h, int i, int j, float v);
@@ -132,6 +145,15 @@ struct GemmArgs {
   int out_vec;  // every destination row is 16-byte aligned (whole 4-float stores)
   int* split_acc;  // tcgen05 GEMM, split last wave: per-part integer accumulators
   int* split_cnt;  //   and per-tile arrival counters (see gemm_tc_split_bytes)
+  // Row levels (nlev > 0): n counts a's permuted rows (whole tiles per level),
+  // row_of[i] is the result row of permuted row i (-1: padding), n_out the
+  // result's rows; lev_tile0 (device, nlev + 1 entries) the first 256-row
+  // tile of every level and the end of the last.
+  int nlev;
+  LevelB lev[kMaxLevels];
+  const int* lev_tile0;
+  const int* row_of;
+  int n_out;
 };
 
 __device__ __forceinline__ void store_out(const GemmArgs& g, int h, int i, int j, float v) {
@@ -147,6 +169,9 @@ cudaError_t launch_build_tables(const int32_t* ra, int n_ra, const int32_t* rb, 
 cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t st);
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st);
 bool gemm_tc_supported(const GemmArgs& g);
+// The row-level GEMM (GemmArgs.nlev > 0).
+cudaError_t launch_gemm_tc_levels(const GemmArgs& g, cudaStream_t st);
+bool gemm_tc_levels_supported(const GemmArgs& g);
 // Workspace of the tcgen05 GEMM's split last wave for this shape on the
 // current device (0 when the last wave is not split); the counters sit at
 // byte offset gemm_tc_split_cnt_offset of that block.

@@ -17,9 +17,9 @@ __device__ __forceinline__ float load_x(const QuantArgs& q, size_t row, int j) {
   return x;
 }
 
-__device__ __forceinline__ int16_t encode(const QuantArgs& q, int j, int boundary, float sgn) {
-  int v = boundary < q.vcap ? boundary : q.vcap;
-  if (q.ktab) v = __ldg(q.ktab + (size_t)__ldg(q.amap + j) * (q.vcap + 1) + v);
+__device__ __forceinline__ int16_t encode(const LevelQ& lq, int j, int boundary, float sgn) {
+  int v = boundary < lq.vcap ? boundary : lq.vcap;
+  if (lq.ktab) v = __ldg(lq.ktab + (size_t)__ldg(lq.amap + j) * (lq.vcap + 1) + v);
   return (int16_t)(sgn < 0.f ? -v : v);
 }
 
@@ -231,37 +231,37 @@ __global__ void tensor_params_kernel(const float* __restrict__ stats_a, int rows
 // One element of the non-chunked recipes: the quantised value's boundary
 // (through the k-table for operand a) with its sign, as the GEMM operand.
 template <int R>
-__device__ __forceinline__ int16_t quant_one(const QuantArgs& q, int j, float x, float sc, float inv, float zp,
-                                            float qf, float& rsum) {
+__device__ __forceinline__ int16_t quant_one(const QuantArgs& q, const LevelQ& lq, int j, float x, float sc, float inv,
+                                            float zp, float qf, float& rsum) {
   {
     int bnd;
     float sgn = 1.f;
     if (R == Q_TENSOR_BIP || R == Q_HEAD_BIP) {
       // fused.py:94-106 / 265-273: clamp(rint(x * inv), [qmin, q]); rint(|xc| * G/q)
       const float xc = fclamp(frint(fmul(x, inv)), q.qmin, qf);
-      bnd = (int)frint(fmul(fabsf(xc), q.ratio));
+      bnd = (int)frint(fmul(fabsf(xc), lq.ratio));
       sgn = xc;
     } else if (R == Q_TENSOR_UNI) {
       // fused.py:84, 98, 114-121: clamp(rint(x * inv + zp), 0, q)
       const float xc = fclamp(frint(fadd(fmul(x, inv), zp)), 0.f, qf);
-      bnd = (int)frint(fmul(xc, q.ratio));
+      bnd = (int)frint(fmul(xc, lq.ratio));
       rsum = fadd(rsum, xc);
     } else if (R == Q_GROUP_SYM) {
       // grouped.py:51 + kernels.py:1679: clamp(round(x / s), +-q); round(|xi| * G / q)
       const float xi = fclamp(frint(fdiv(x, sc)), -qf, qf);
-      bnd = (int)frint(fdiv(fmul(fabsf(xi), (float)q.G), qf));
+      bnd = (int)frint(fdiv(fmul(fabsf(xi), (float)lq.G), qf));
       sgn = xi;
     } else if (R == Q_BATCH_SYM) {
       // grouped.py:148/156 + kernels.py:1864: round(|xi| * fl32(G / q))
       const float xi = fclamp(frint(fdiv(x, sc)), -qf, qf);
-      bnd = (int)frint(fmul(fabsf(xi), q.ratio));
+      bnd = (int)frint(fmul(fabsf(xi), lq.ratio));
       sgn = xi;
     } else {  // Q_GROUP_ASYM: grouped.py:131 + kernels.py:1685
       const float xi = fclamp(frint(fadd(fdiv(x, sc), zp)), 0.f, qf);
-      bnd = (int)frint(fdiv(fmul(xi, (float)q.G), qf));
+      bnd = (int)frint(fdiv(fmul(xi, (float)lq.G), qf));
       rsum = fadd(rsum, xi);
     }
-    return encode(q, j, bnd, sgn);
+    return encode(lq, j, bnd, sgn);
   }
 }
 
@@ -271,6 +271,31 @@ __global__ void quant_rows_kernel(QuantArgs q) {
   if (row >= q.rows) return;
   const float qf = (float)q.q;
   int16_t* out = q.out16;  // blocked [d/8][rows][8] layout (blk_idx)
+  // the source row and the grid it is quantised on (row levels: its level's)
+  int src = row;
+  LevelQ lq{q.ratio, q.G, q.vcap, q.ktab, q.amap};
+  if (q.row_of) {
+    src = __ldg(q.row_of + row);
+    int lv = q.nlev - 1;
+    for (int l = 0; l < q.nlev; ++l)
+      if ((row >> 8) < __ldg(q.lev_tile0 + l + 1)) {
+        lv = l;
+        break;
+      }
+    lq = q.lq[lv];
+    if (src < 0) {  // padding row of a level's last tile: a zero operand
+      const int nch = R == Q_ROWCHUNK_BIP ? cdiv(q.d, q.chunk_d) : 0;
+      for (int c = lane; c < nch; c += 32) q.chunk_scale[(size_t)c * q.rows + row] = 0.f;
+      for (int jb = lane; jb < d8(q.d); jb += 32)
+        *reinterpret_cast<uint4*>(out + blk_idx(q.rows, row, 8 * jb)) = make_uint4(0, 0, 0, 0);
+      if (lane == 0) {
+        if (q.row_scale) q.row_scale[row] = 0.f;
+        if (q.row_zp) q.row_zp[row] = 0.f;
+        if (q.row_sum) q.row_sum[row] = 0.f;
+      }
+      return;
+    }
+  }
 
   if (R == Q_ROWCHUNK_BIP) {
     // fused_quant_kernel PER_ROW bipolar on every chunk (fused.py:65-81, 98-112)
@@ -278,15 +303,15 @@ __global__ void quant_rows_kernel(QuantArgs q) {
     for (int c = 0; c < nch; ++c) {
       const int j0 = c * q.chunk_d, j1 = min(j0 + q.chunk_d, q.d);
       float am = 0.f;
-      for (int j = j0 + lane; j < j1; j += 32) am = fmaxf(am, fabsf(load_x(q, row, j)));
+      for (int j = j0 + lane; j < j1; j += 32) am = fmaxf(am, fabsf(load_x(q, src, j)));
       am = fmaxf(warp_max(am), 1e-5f);
       const float sc = fdiv(am, qf);
       const float inv = fdiv(1.0f, sc);
       if (lane == 0) q.chunk_scale[(size_t)c * q.rows + row] = sc;
       for (int j = j0 + lane; j < j1; j += 32) {
-        const float xc = fclamp(frint(fmul(load_x(q, row, j), inv)), -qf, qf);
-        const int bnd = (int)frint(fmul(fabsf(xc), q.ratio));
-        out[blk_idx(q.rows, row, j)] = encode(q, j, bnd, xc);
+        const float xc = fclamp(frint(fmul(load_x(q, src, j), inv)), -qf, qf);
+        const int bnd = (int)frint(fmul(fabsf(xc), lq.ratio));
+        out[blk_idx(q.rows, row, j)] = encode(lq, j, bnd, xc);
       }
     }
     return;
@@ -301,7 +326,7 @@ __global__ void quant_rows_kernel(QuantArgs q) {
   } else if (q.self_stats) {
     // G == 1: the row is its own group (grouped.py:46-47, 111-115)
     float am, mx, mn;
-    row_minmax(q, row, lane, am, mx, mn);
+    row_minmax(q, src, lane, am, mx, mn);
     if (R == Q_GROUP_ASYM) {
       sc = fdiv(fmaxf(fsub(mx, mn), 1e-5f), qf);
       zp = fclamp(frint(fdiv(-mn, sc)), 0.f, qf);
@@ -326,8 +351,8 @@ __global__ void quant_rows_kernel(QuantArgs q) {
     const int j0 = 8 * jb;
     float xs[8];
     if (q.vec && j0 + 8 <= q.d) {
-      const float4* src = reinterpret_cast<const float4*>(q.x + (size_t)row * q.d + j0);
-      const float4 u = __ldg(src), w = __ldg(src + 1);
+      const float4* sp = reinterpret_cast<const float4*>(q.x + (size_t)src * q.d + j0);
+      const float4 u = __ldg(sp), w = __ldg(sp + 1);
       xs[0] = u.x; xs[1] = u.y; xs[2] = u.z; xs[3] = u.w;
       xs[4] = w.x; xs[5] = w.y; xs[6] = w.z; xs[7] = w.w;
       if (q.smooth) {
@@ -339,7 +364,7 @@ __global__ void quant_rows_kernel(QuantArgs q) {
       }
     } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) xs[e] = j0 + e < q.d ? load_x(q, row, j0 + e) : 0.f;
+      for (int e = 0; e < 8; ++e) xs[e] = j0 + e < q.d ? load_x(q, src, j0 + e) : 0.f;
     }
     uint32_t packed[4];
 #pragma unroll
@@ -347,7 +372,7 @@ __global__ void quant_rows_kernel(QuantArgs q) {
       const int j = j0 + e;
       const float x = xs[e];
       int16_t code = 0;
-      if (j < q.d) code = quant_one<R>(q, j, x, sc, inv, zp, qf, rsum);
+      if (j < q.d) code = quant_one<R>(q, lq, j, x, sc, inv, zp, qf, rsum);
       if (e & 1)
         packed[e >> 1] |= (uint32_t)(uint16_t)code << 16;
       else
@@ -362,8 +387,74 @@ __global__ void quant_rows_kernel(QuantArgs q) {
 }
 
 // --------------------------------------------------------------------------
+// row levels: a's rows grouped by level, each level padded to whole tiles
+// --------------------------------------------------------------------------
+
+// One block. Counts the rows of every level, lays the levels out in tiles of
+// 256 rows (level l from tile lev_tile0[l]) and scatters the row indices
+// stably: within a level, rows keep their order (the order in which a
+// caller's a[rows] would gather them). Rows whose level is out of range are
+// left out and recorded as a device error.
+__global__ void level_perm_kernel(const int32_t* __restrict__ row_level, int n, int nlev, int n_pad,
+                                  int* __restrict__ row_of, int* __restrict__ lev_tile0) {
+  __shared__ int cnt[kMaxLevels], base[kMaxLevels], wcnt[32][kMaxLevels];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  for (int i = tid; i < n_pad; i += blockDim.x) row_of[i] = -1;
+  if (tid < kMaxLevels) cnt[tid] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += blockDim.x) {
+    const int l = __ldg(row_level + i);
+    if (l >= 0 && l < nlev) atomicAdd(&cnt[l], 1);
+    else record_error(SCMP_ERR_INVALID_ARG, 40);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int t = 0;
+    for (int l = 0; l < nlev; ++l) {
+      lev_tile0[l] = t;
+      base[l] = 256 * t;
+      t += cdiv(cnt[l], 256);
+    }
+    lev_tile0[nlev] = t;
+  }
+  __syncthreads();
+  for (int c0 = 0; c0 < n; c0 += blockDim.x) {
+    const int i = c0 + tid;
+    const int l = i < n ? __ldg(row_level + i) : -1;
+    const bool ok = l >= 0 && l < nlev;
+    int rank = 0;
+#pragma unroll
+    for (int k = 0; k < kMaxLevels; ++k) {
+      const unsigned bal = __ballot_sync(0xFFFFFFFFu, ok && l == k);
+      if (l == k) rank = __popc(bal & ((1u << lane) - 1u));
+      if (lane == 0) wcnt[warp][k] = __popc(bal);
+    }
+    __syncthreads();
+    if (ok) {
+      int off = 0;
+      for (int w = 0; w < warp; ++w) off += wcnt[w][l];
+      row_of[base[l] + off + rank] = i;
+    }
+    __syncthreads();
+    if (tid < nlev) {
+      int tot = 0;
+      for (int w = 0; w < nw; ++w) tot += wcnt[w][tid];
+      base[tid] += tot;
+    }
+    __syncthreads();
+  }
+}
+
+// --------------------------------------------------------------------------
 // host launchers
 // --------------------------------------------------------------------------
+
+cudaError_t launch_level_perm(const int32_t* row_level, int n, int nlev, int n_pad, int* row_of, int* lev_tile0,
+                              cudaStream_t st) {
+  level_perm_kernel<<<1, 1024, 0, st>>>(row_level, n, nlev, n_pad, row_of, lev_tile0);
+  count_launch();
+  return cudaGetLastError();
+}
 
 static inline dim3 warp_grid(int rows) { return dim3(cdiv(rows, 8)); }
 

@@ -17,6 +17,15 @@ enum QuantRecipe {
 
 enum GroupRecipe { GP_SYM = 0, GP_ASYM = 1, GP_HEAD = 2 };
 
+// Grid of one row level: boundary scale, grid, table (operand a's k-table).
+struct LevelQ {
+  float ratio;          // fl32(G / q) of the multiply-form boundary
+  int G;                // grid levels of the divide-form boundary
+  int vcap;
+  const int16_t* ktab;  // operand a: boundary -> k, or NULL
+  const int32_t* amap;
+};
+
 struct QuantArgs {
   const float* x;  // (rows, d) float32, rows = batch * rows_per_batch
   int rows, d, rows_per_batch;
@@ -41,6 +50,13 @@ struct QuantArgs {
   const int32_t* amap;
   int vcap;
   float* row_sum;       // (rows,) unipolar, or NULL
+  // Row levels (operand a): row i of the output is row row_of[i] of x (-1:
+  // padding, written as zeros), quantised on the grid of its level, the level
+  // whose rows [256 * lev_tile0[l], 256 * lev_tile0[l + 1]) hold i.
+  const int* row_of;
+  const int* lev_tile0;
+  int nlev;
+  LevelQ lq[kMaxLevels];
 };
 
 cudaError_t launch_row_stats(const QuantArgs& q, float* stats, cudaStream_t st);
@@ -49,5 +65,10 @@ cudaError_t launch_group_params(const float* stats, int batch, int rpb, int G, i
 cudaError_t launch_tensor_params(const float* sa, int ra, const float* sb, int rb, int d, int q,
                                  int unipolar, const double* ranges, float* scal, cudaStream_t st);
 cudaError_t launch_quant_rows(int recipe, const QuantArgs& q, cudaStream_t st);
+// Permutation of a's rows by level (rows of one level in increasing order,
+// every level padded to whole 256-row tiles): row_of (n_pad entries) and
+// lev_tile0 (nlev + 1 entries) on the device, from row_level (n,).
+cudaError_t launch_level_perm(const int32_t* row_level, int n, int nlev, int n_pad, int* row_of, int* lev_tile0,
+                              cudaStream_t st);
 
 }  // namespace scmp

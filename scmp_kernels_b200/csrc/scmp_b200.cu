@@ -5,5 +5,6 @@
 #include "gemm_simt.cu"
 #include "gemm_tc.cu"
 #include "api.cu"
+#include "levels.cu"
 #include "quant_ref.cu"
 #include "noalloc.cu"

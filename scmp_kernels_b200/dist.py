@@ -207,7 +207,10 @@ def sc_matmul_sharded(a: torch.Tensor, b_shard: torch.Tensor, rows_total: int,
         if ranges is None:
             mm = matmul
             if mm is None:
-                from .sc.matmul import sc_matmul as mm
+                if "row_levels" in kw:  # a stream length per row of a: sc_matmul_levels
+                    from .sc.levels import sc_matmul_levels as mm
+                else:
+                    from .sc.matmul import sc_matmul as mm
             return mm(a, b_shard, granularity, **kw)
         if matmul is not None:
             return matmul(a, b_shard, granularity, ranges=ranges, **kw)

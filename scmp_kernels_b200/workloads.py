@@ -120,3 +120,15 @@ def mp_row_levels(a: torch.Tensor, group: int = 4,
         tail = torch.arange(n_groups * group, rows, device=a.device)
         out[levels[-1]] = torch.cat([out[levels[-1]], tail])
     return out
+
+
+def mp_row_level_index(a: torch.Tensor, group: int = 4, levels=(256, 128, 64)):
+    """The assignment of ``mp_row_levels`` as ``(row_levels, stoc_len_levels)``:
+    the level index of every row of a (int32, on a's device; the form of the
+    reference's ``RowAssignment.row_levels``) and the stream length of every
+    level, the arguments of ``sc_matmul_levels``."""
+    lv = mp_row_levels(a, group, levels)
+    rl = torch.empty(a.shape[0], dtype=torch.int32, device=a.device)
+    for i, L in enumerate(levels):
+        rl[lv[L]] = i
+    return rl, [int(L) for L in levels]

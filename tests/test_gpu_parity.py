@@ -195,6 +195,33 @@ def test_split_last_wave_matches_whole_tiles(shape, kw, single, i8, monkeypatch,
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("shape,kw", [
+    ((2048, 11008, 1024), dict(granularity="per_row", sc_prec=8)),                # 8 bands, 23 tiles each
+    ((1800, 3000, 640), dict(granularity="per_row", mode="unipolar", sc_prec=6, stoc_len=64)),  # ragged
+    ((5, 197, 197, 640), dict(granularity="per_head", sc_prec=8)),                # one band per head
+])
+@pytest.mark.parametrize("group", ["3", "8"])
+def test_band_grouped_tile_order_matches_default(shape, kw, group, monkeypatch, env_vars):
+    """Tiles taken in groups of bands of a (each b tile for every band of a
+    group, SCMP_TC_BAND_GROUP) give the bits of the band-by-band order, the
+    split last wave included."""
+    env_vars({})
+    g = torch.Generator(device=DEV).manual_seed(6)
+    if len(shape) == 4:
+        bh, n, m, d = shape
+        a, b = torch.randn(bh, n, d, device=DEV, generator=g), torch.randn(bh, m, d, device=DEV, generator=g)
+    else:
+        n, m, d = shape
+        a, b = torch.randn(n, d, device=DEV, generator=g), torch.randn(m, d, device=DEV, generator=g) * 0.05
+    monkeypatch.setattr(K, "_FORCE_SIMT", False)
+    monkeypatch.setenv("SCMP_TC_BAND_GROUP", "1")
+    y1 = sc_matmul(a, b, **kw)
+    monkeypatch.setenv("SCMP_TC_BAND_GROUP", group)
+    yg = sc_matmul(a, b, **kw)
+    assert torch.equal(y1, yg)
+    assert _lib.device_error() == 0
+
+
 @pytest.mark.parametrize("gran,shape", [("per_row", (70, 300, 500)), ("per_tensor", (33, 90, 130)),
                                         ("per_head", (3, 40, 50, 64))])
 @pytest.mark.parametrize("simt", [False, True])
