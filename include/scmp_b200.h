@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define SCMP_ABI_VERSION 3
+#define SCMP_ABI_VERSION 4
 
 enum scmp_status {
   SCMP_OK = 0,
@@ -151,6 +151,11 @@ typedef struct scmp_matmul_desc {
   int out_ld;              /* row stride of the destinations, >= m                */
   long long out_offset;    /* element offset of (0, 0, 0) in every destination    */
   const uint32_t* pattern4; /* from scmp_build_tables, or NULL (int8 operands)     */
+  /* With n_out_peers > 1: 1 + the index in out_peers of the destination in this
+   * device's own memory, or 0 if none is. When set, the wide-tile GEMM stores
+   * each finished tile there first, frees the tile's accumulator, and copies
+   * the tile to the other destinations while the next tile's MMAs run. */
+  int out_self;
 } scmp_matmul_desc;
 
 #define SCMP_MAX_OUT_PEERS 8

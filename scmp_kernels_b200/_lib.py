@@ -27,7 +27,7 @@ BIPOLAR, UNIPOLAR = 0, 1
 FLAG_FORCE_SIMT = 0x1
 FLAG_NO_SPLIT = 0x2
 FLAG_B_READY = 0x4
-ABI_VERSION = 3
+ABI_VERSION = 4
 MAX_OUT_PEERS = 8
 
 c_int, c_void_p, c_size_t, c_float, c_double = (ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
@@ -44,7 +44,7 @@ class MatmulDesc(ctypes.Structure):
         ("ktab", c_void_p), ("pattern", c_void_p), ("amap", c_void_p), ("bmap", c_void_p),
         ("vcap", c_int), ("lp", c_int), ("flags", c_int), ("tensor_ranges", c_void_p),
         ("out_peers", c_void_p), ("n_out_peers", c_int), ("out_ld", c_int), ("out_offset", ctypes.c_longlong),
-        ("pattern4", c_void_p),
+        ("pattern4", c_void_p), ("out_self", c_int),
     ]
 
 

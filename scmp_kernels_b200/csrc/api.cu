@@ -323,6 +323,7 @@ int scmp_sc_matmul(const scmp_matmul_desc* d, void* workspace, size_t workspace_
     g.out_ld = d->m;
   }
   g.out_vec = g.out_off % 4 == 0 && g.out_ld % 4 == 0;
+  g.out_self = d->n_out_peers > 1 && d->out_self >= 1 && d->out_self <= d->n_out_peers ? d->out_self : 0;
   for (int k = 0; k < g.nouts; ++k) g.out_vec &= (reinterpret_cast<uintptr_t>(g.outs[k]) & 15) == 0;
   g.split_acc = p.split_acc;
   g.split_cnt = p.split_cnt;

@@ -282,8 +282,10 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
 // lane) instead of 32 scattered words: full lines for local HBM and for a
 // peer's memory over NVLink alike. Chunks are XOR-swizzled by row, so both
 // the row-wise writes and the segment-wise reads are free of bank conflicts.
+// only >= 0: store to destination `only` alone (the tile's peer copies are
+// made later by copy_rows_to_peers).
 __device__ __forceinline__ void store_rows32(const GemmArgs& g, uint32_t stg, int bh, int ia0, int ib0, int m_end,
-                                             const uint32_t (&v)[32], int lane) {
+                                             const uint32_t (&v)[32], int lane, int only = -1) {
 #pragma unroll
   for (int k = 0; k < 8; ++k)
     st_shared_v4(stg + lane * 128 + ((k ^ (lane & 7)) << 4), v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
@@ -302,7 +304,7 @@ __device__ __forceinline__ void store_rows32(const GemmArgs& g, uint32_t stg, in
       const long long idx = g.out_off + ((long long)bh * (g.row_of ? g.n_out : g.n) + orow) * g.out_ld + ib;
       const bool whole = g.out_vec && ib + 3 < m_end;
 #pragma unroll 1
-      for (int k = 0; k < g.nouts; ++k) {
+      for (int k = only < 0 ? 0 : only; k < (only < 0 ? g.nouts : only + 1); ++k) {
         float* o = g.outs[k] + idx;
         if (whole) {
           *reinterpret_cast<uint4*>(o) = x;
@@ -316,6 +318,51 @@ __device__ __forceinline__ void store_rows32(const GemmArgs& g, uint32_t stg, in
     }
   }
   __syncwarp();
+}
+
+// Copies the tile block rows [ia0, ia0 + nrows) x columns [ib0, m_end) of
+// batch entry bh from destination `self` (this device's memory, where the
+// epilogue stored it) to every other destination, one warp over the rows
+// r0, r0 + rstep, ...: 16 bytes per lane, a row segment per instruction.
+// Reads bypass L1 (the rows were written by other warps of the CTA).
+__device__ __forceinline__ void copy_rows_to_peers(const GemmArgs& g, int self, int bh, int ia0, int nrows, int ib0,
+                                                   int m_end, int r0, int rstep, int lane) {
+  const int ncol = m_end - ib0;
+  const long long rows_base = (long long)bh * (g.row_of ? g.n_out : g.n);
+#pragma unroll 1
+  for (int r = r0; r < nrows; r += rstep) {
+    const int ia = ia0 + r;
+    int orow = ia < g.n ? ia : -1;
+    if (g.row_of && orow >= 0) orow = __ldg(g.row_of + ia);
+    if (orow < 0) continue;
+    const long long base = g.out_off + (rows_base + orow) * g.out_ld + ib0;
+    const float* src = g.outs[self] + base;
+    if (g.out_vec) {
+#pragma unroll 1
+      for (int c = 4 * lane; c < ncol; c += 128) {
+        if (c + 3 < ncol) {
+          const float4 x = __ldcg(reinterpret_cast<const float4*>(src + c));
+#pragma unroll 1
+          for (int k = 0; k < g.nouts; ++k)
+            if (k != self) *reinterpret_cast<float4*>(g.outs[k] + base + c) = x;
+        } else {
+          for (int e = c; e < ncol; ++e) {
+            const float x = __ldcg(src + e);
+            for (int k = 0; k < g.nouts; ++k)
+              if (k != self) g.outs[k][base + e] = x;
+          }
+        }
+      }
+    } else {
+#pragma unroll 1
+      for (int c = lane; c < ncol; c += 32) {
+        const float x = __ldcg(src + c);
+#pragma unroll 1
+        for (int k = 0; k < g.nouts; ++k)
+          if (k != self) g.outs[k][base + c] = x;
+      }
+    }
+  }
 }
 
 // Integer value of an accumulator word: int32 for kind::i8, a float32 holding
@@ -576,6 +623,14 @@ __device__ __forceinline__ bool produce_item(const GemmArgs& g, const Sched& sc,
             nb_hi = __ldg(bmsrc + 2 * (blk0 + blk + 1) + 1);
           }
         }
+        if constexpr (NSPB <= 2) {
+          // short streams: a block is one or two stages, so the operand load
+          // one block ahead has little time to arrive; the row's block
+          // PF blocks ahead is fetched into L2 now
+          constexpr int PF = NSPB == 1 ? 4 : 2;
+          if (valid && blk + PF < nblk)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(kvsrc + (size_t)(blk0 + blk + PF) * R + grow));
+        }
         const int jmax = min(NSPB, nst - blk * NSPB);
         // UNR (e2m1 long tiles and the chunked path): the block's stages are
         // unrolled, so every dimension index below is a compile-time constant
@@ -780,6 +835,9 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
   auto accf_bar = [&](int b) { return bar_base + 8u * (2 * NST + b); };
   auto acce_bar = [&](int b) { return bar_base + 8u * (2 * NST + 2 + b); };
   const uint32_t drain_bar = bar_base + 8u * (2 * NST + 4);
+  // wide tiles with the result's peer copies deferred (GemmArgs.out_self):
+  // the epilogue warps' local stores of a tile are complete
+  const uint32_t cpy_bar = bar_base + 8u * (2 * NST + 5);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + C::SB_BYTES + 128);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + C::SB_BYTES + 136);
   volatile int* split_flag = reinterpret_cast<volatile int*>(gbase + NST * C::STAGE_BYTES + C::STG_BYTES + C::SB_BYTES + 144);
@@ -801,6 +859,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
         mbar_init(acce_bar(b), C::NCTA * 4);  // one arrival per epilogue warp of the tile
       }
       mbar_init(drain_bar, 1);
+      mbar_init(cpy_bar, 4);  // one arrival per epilogue warp of the CTA
       *abort_flag = 0;
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -934,7 +993,8 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16);
     const uint32_t stg = stg_base + (uint32_t)q * (32 * 32 * 4);  // this warp's staging area
-    uint32_t uc = 0, mit = 0;
+    uint32_t uc = 0, mit = 0, cpy_phase = 0;
+    const bool deferred = C::MERGED && g.out_self > 0;
     for (int w = tile0; w < sc.nwork; w += tstep) {
       const Work wk = work_of(sc, w, g.d);
       if (units_of(sc, wk) == 0) continue;  // empty tail piece
@@ -1109,11 +1169,28 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
               fin[16 * h + j] = __float_as_uint(v);
             }
           }
-          store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, m_end, fin, lane);
+          store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, m_end, fin, lane, deferred ? g.out_self - 1 : -1);
+        }
+        if (deferred) {  // this warp's rows are in this device's destination
+          __threadfence_block();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(cpy_bar);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar(buf), rank);
+        if (deferred) {
+          // The accumulator is free and the next tile's MMAs can start; the
+          // other epilogue warps copy the CTA's 128 rows of this tile to the
+          // other destinations (over NVLink) meanwhile, once all four warps
+          // have stored their rows. The first warp (the MMA issuer in the
+          // leader CTA) goes straight on.
+          if (q != 0) {
+            if (!mbar_wait(cpy_bar, cpy_phase & 1, abort_flag, 7)) goto epi_out;
+            copy_rows_to_peers(g, g.out_self - 1, bh, a0 + (int)rank * C::BM, C::BM, b0, m_end, q - 1, 3, lane);
+          }
+          ++cpy_phase;
+        }
       }
     }
   epi_out:
@@ -1289,8 +1366,14 @@ static Sched make_sched(int batch, int n, int m, int d, int unit_d, Variant v, i
     }
   }
   s.nwork = s.full + (s.tail_w > 0 ? 2 * s.workers : 0);
+  // Tile order: for wide tiles, groups of eight 256-row bands of a
+  // (SCMP_TC_BAND_GROUP=g in the environment selects g; 1 is band after
+  // band). With eight bands the tiles in flight share about nine b tiles'
+  // operand rows and the group's a rows in L2 (config 5, whose b operand is
+  // 470 MB: GEMM 37.7 -> 36.0 ms). Narrow tiles keep the band order (config
+  // 4's row-level call was slower grouped: 2.92 -> 3.28 ms).
   const char* bg = getenv("SCMP_TC_BAND_GROUP");
-  s.band_group = bg ? atoi(bg) : 1;
+  s.band_group = bg ? atoi(bg) : (v.wide ? 8 : 1);
   if (s.band_group < 1) s.band_group = 1;
   return s;
 }

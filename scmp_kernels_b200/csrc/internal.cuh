@@ -143,6 +143,7 @@ struct GemmArgs {
   long long out_off;
   int out_ld;
   int out_vec;  // every destination row is 16-byte aligned (whole 4-float stores)
+  int out_self; // 1 + index of the destination in this device's memory (0: none); see store_rows32
   int* split_acc;  // tcgen05 GEMM, split last wave: per-part integer accumulators
   int* split_cnt;  //   and per-tile arrival counters (see gemm_tc_split_bytes)
   // Row levels (nlev > 0): n counts a's permuted rows (whole tiles per level),

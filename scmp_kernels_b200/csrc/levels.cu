@@ -159,6 +159,7 @@ int scmp_sc_matmul_levels(const scmp_matmul_desc* d, const scmp_level_desc* lv, 
     g.out_ld = d->m;
   }
   g.out_vec = g.out_off % 4 == 0 && g.out_ld % 4 == 0;
+  g.out_self = d->n_out_peers > 1 && d->out_self >= 1 && d->out_self <= d->n_out_peers ? d->out_self : 0;
   for (int k = 0; k < g.nouts; ++k) g.out_vec &= (reinterpret_cast<uintptr_t>(g.outs[k]) & 15) == 0;
   for (int l = 0; l < nlev; ++l) {
     g.lev[l].vb = p.vb[l];

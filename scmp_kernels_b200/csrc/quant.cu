@@ -230,37 +230,56 @@ __global__ void tensor_params_kernel(const float* __restrict__ stats_a, int rows
 
 // One element of the non-chunked recipes: the quantised value's boundary
 // (through the k-table for operand a) with its sign, as the GEMM operand.
+// Boundary of a quantised magnitude m (an integer held in a float) on the grid
+// of lq: the divide form of the grouped recipes, round(m * G / q)
+// (kernels.py:1679, 1685), or the multiply form round(m * fl32(G / q)) of the
+// others (quant/fused.py:98-106, kernels.py:1864).
+template <int R>
+__device__ __forceinline__ int bnd_of(const LevelQ& lq, float m, float qf) {
+  if (R == Q_GROUP_SYM || R == Q_GROUP_ASYM) return (int)frint(fdiv(fmul(m, (float)lq.G), qf));
+  return (int)frint(fmul(m, lq.ratio));
+}
+
+// Magnitudes 0 .. kBndTab - 1 whose boundaries quant_rows_kernel tabulates in
+// shared memory (q_max + 1 < kBndTab; the magnitude of a clamped value is an
+// integer in [0, q_max + 1]), so that an element costs one table read instead
+// of the boundary's multiply, divide and rounding. The table holds bnd_of's
+// own results, so the boundaries are the same.
+constexpr int kBndTab = 258;  // q_max <= 256: sc_prec up to 8 (4 KB of shared memory for four grids)
+
+// tab: the boundary table of lq's grid, or NULL to compute the boundary.
 template <int R>
 __device__ __forceinline__ int16_t quant_one(const QuantArgs& q, const LevelQ& lq, int j, float x, float sc, float inv,
-                                            float zp, float qf, float& rsum) {
+                                            float zp, float qf, float& rsum, const int* tab = nullptr) {
   {
-    int bnd;
+    float mag;
     float sgn = 1.f;
     if (R == Q_TENSOR_BIP || R == Q_HEAD_BIP) {
       // fused.py:94-106 / 265-273: clamp(rint(x * inv), [qmin, q]); rint(|xc| * G/q)
       const float xc = fclamp(frint(fmul(x, inv)), q.qmin, qf);
-      bnd = (int)frint(fmul(fabsf(xc), lq.ratio));
+      mag = fabsf(xc);
       sgn = xc;
     } else if (R == Q_TENSOR_UNI) {
       // fused.py:84, 98, 114-121: clamp(rint(x * inv + zp), 0, q)
       const float xc = fclamp(frint(fadd(fmul(x, inv), zp)), 0.f, qf);
-      bnd = (int)frint(fmul(xc, lq.ratio));
+      mag = xc;
       rsum = fadd(rsum, xc);
     } else if (R == Q_GROUP_SYM) {
       // grouped.py:51 + kernels.py:1679: clamp(round(x / s), +-q); round(|xi| * G / q)
       const float xi = fclamp(frint(fdiv(x, sc)), -qf, qf);
-      bnd = (int)frint(fdiv(fmul(fabsf(xi), (float)lq.G), qf));
+      mag = fabsf(xi);
       sgn = xi;
     } else if (R == Q_BATCH_SYM) {
       // grouped.py:148/156 + kernels.py:1864: round(|xi| * fl32(G / q))
       const float xi = fclamp(frint(fdiv(x, sc)), -qf, qf);
-      bnd = (int)frint(fmul(fabsf(xi), lq.ratio));
+      mag = fabsf(xi);
       sgn = xi;
     } else {  // Q_GROUP_ASYM: grouped.py:131 + kernels.py:1685
       const float xi = fclamp(frint(fadd(fdiv(x, sc), zp)), 0.f, qf);
-      bnd = (int)frint(fdiv(fmul(xi, (float)lq.G), qf));
+      mag = xi;
       rsum = fadd(rsum, xi);
     }
+    const int bnd = tab ? tab[(int)mag] : bnd_of<R>(lq, mag, qf);
     return encode(lq, j, bnd, sgn);
   }
 }
@@ -268,12 +287,24 @@ __device__ __forceinline__ int16_t quant_one(const QuantArgs& q, const LevelQ& l
 template <int R>
 __global__ void quant_rows_kernel(QuantArgs q) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (row >= q.rows) return;
   const float qf = (float)q.q;
+  // boundary tables of the grids (one, or one per row level), see kBndTab
+  __shared__ int s_bnd[kMaxLevels][kBndTab];
+  const bool use_tab = q.q + 1 < kBndTab;
+  if (use_tab) {
+    const int nt = q.row_of ? q.nlev : 1;
+    for (int l = 0; l < nt; ++l) {
+      const LevelQ L = q.row_of ? q.lq[l] : LevelQ{q.ratio, q.G, q.vcap, q.ktab, q.amap};
+      for (int i = threadIdx.x; i <= q.q + 1; i += blockDim.x) s_bnd[l][i] = bnd_of<R>(L, (float)i, qf);
+    }
+    __syncthreads();
+  }
+  if (row >= q.rows) return;
   int16_t* out = q.out16;  // blocked [d/8][rows][8] layout (blk_idx)
   // the source row and the grid it is quantised on (row levels: its level's)
   int src = row;
   LevelQ lq{q.ratio, q.G, q.vcap, q.ktab, q.amap};
+  const int* tab = use_tab ? s_bnd[0] : nullptr;
   if (q.row_of) {
     src = __ldg(q.row_of + row);
     int lv = q.nlev - 1;
@@ -283,6 +314,7 @@ __global__ void quant_rows_kernel(QuantArgs q) {
         break;
       }
     lq = q.lq[lv];
+    if (use_tab) tab = s_bnd[lv];
     if (src < 0) {  // padding row of a level's last tile: a zero operand
       const int nch = R == Q_ROWCHUNK_BIP ? cdiv(q.d, q.chunk_d) : 0;
       for (int c = lane; c < nch; c += 32) q.chunk_scale[(size_t)c * q.rows + row] = 0.f;
@@ -310,7 +342,7 @@ __global__ void quant_rows_kernel(QuantArgs q) {
       if (lane == 0) q.chunk_scale[(size_t)c * q.rows + row] = sc;
       for (int j = j0 + lane; j < j1; j += 32) {
         const float xc = fclamp(frint(fmul(load_x(q, src, j), inv)), -qf, qf);
-        const int bnd = (int)frint(fmul(fabsf(xc), lq.ratio));
+        const int bnd = tab ? tab[(int)fabsf(xc)] : bnd_of<R>(lq, fabsf(xc), qf);
         out[blk_idx(q.rows, row, j)] = encode(lq, j, bnd, xc);
       }
     }
@@ -372,7 +404,7 @@ __global__ void quant_rows_kernel(QuantArgs q) {
       const int j = j0 + e;
       const float x = xs[e];
       int16_t code = 0;
-      if (j < q.d) code = quant_one<R>(q, lq, j, x, sc, inv, zp, qf, rsum);
+      if (j < q.d) code = quant_one<R>(q, lq, j, x, sc, inv, zp, qf, rsum, tab);
       if (e & 1)
         packed[e >> 1] |= (uint32_t)(uint16_t)code << 16;
       else
@@ -383,6 +415,199 @@ __global__ void quant_rows_kernel(QuantArgs q) {
   if (q.row_sum) {
     rsum = warp_sum(rsum);
     if (lane == 0) q.row_sum[row] = rsum;
+  }
+}
+
+// --------------------------------------------------------------------------
+// quantisers, staged: RT rows per block of 256 threads, one pass over HBM
+// --------------------------------------------------------------------------
+
+// The non-chunked recipes of quant_rows_kernel with RT consecutive rows per
+// block: the rows are copied to shared memory with cp.async (16-byte copies,
+// all in flight at once; rows of a misaligned or ragged x are loaded element
+// by element), the row statistics are reduced from shared memory, and the
+// operand is written one block of eight dimensions for each of the RT rows at
+// a time, so that each store instruction fills RT * 16 contiguous bytes of the
+// blocked layout. Smoothing is applied where the values are read. Results are
+// identical to quant_rows_kernel (same per-element recipe, and the row sums
+// add exact integers, in any order).
+template <int R, int RT>
+__global__ void __launch_bounds__(256) quant_tile_kernel(QuantArgs q) {
+  extern __shared__ __align__(16) float xsm[];  // RT rows, stride elements each
+  __shared__ float s_sc[RT], s_inv[RT], s_zp[RT], s_sum[RT];
+  __shared__ int s_src[RT], s_lev[RT];
+  __shared__ float s_red[3][RT][8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row0 = blockIdx.x * RT;
+  const int d4 = (q.d + 3) >> 2;
+  const int stride = 4 * d4 + 4;  // floats; 16 bytes of padding between rows
+  const float qf = (float)q.q;
+  if (tid < RT) {
+    const int row = row0 + tid;
+    int src = row < q.rows ? row : -1;
+    int lv = -1;
+    if (q.row_of && src >= 0) {
+      src = __ldg(q.row_of + row);
+      lv = q.nlev - 1;
+      for (int l = 0; l < q.nlev; ++l)
+        if ((row >> 8) < __ldg(q.lev_tile0 + l + 1)) {
+          lv = l;
+          break;
+        }
+    }
+    s_src[tid] = src;
+    s_lev[tid] = lv;
+    s_sum[tid] = 0.f;
+  }
+  __syncthreads();
+  // stage the rows
+  const bool async = q.vec != 0;
+#pragma unroll
+  for (int r = 0; r < RT; ++r) {
+    const int src = s_src[r];
+    float* dst = xsm + r * stride;
+    if (src < 0) continue;
+    if (async) {
+      const float* gsrc = q.x + (size_t)src * q.d;
+      for (int c = tid; c < d4; c += 256) {
+        const uint32_t sa = smem_u32(dst + 4 * c);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gsrc + 4 * c) : "memory");
+      }
+    } else {
+      for (int j = tid; j < q.d; j += 256) dst[j] = __ldg(q.x + (size_t)src * q.d + j);
+    }
+  }
+  if (async) asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  auto xval = [&](int r, int j) -> float {  // smoothed element j of staged row r
+    float x = xsm[r * stride + j];
+    if (q.smooth) x = q.smooth_div ? fdiv(x, __ldg(q.smooth + j)) : fmul(x, __ldg(q.smooth + j));
+    return x;
+  };
+  // per-row parameters
+  const bool self = (R == Q_GROUP_SYM || R == Q_GROUP_ASYM || R == Q_BATCH_SYM) && q.self_stats;
+  if (self) {
+#pragma unroll
+    for (int r = 0; r < RT; ++r) {
+      float am = 0.f, mx = -INFINITY, mn = INFINITY;
+      if (s_src[r] >= 0)
+        for (int j = tid; j < q.d; j += 256) {
+          const float x = xval(r, j);
+          am = fmaxf(am, fabsf(x));
+          mx = fmaxf(mx, x);
+          mn = fminf(mn, x);
+        }
+      am = warp_max(am);
+      mx = warp_max(mx);
+      mn = warp_min(mn);
+      if (lane == 0) {
+        s_red[0][r][warp] = am;
+        s_red[1][r][warp] = mx;
+        s_red[2][r][warp] = mn;
+      }
+    }
+    __syncthreads();
+  }
+  if (tid < RT) {
+    const int r = tid, row = row0 + r;
+    float sc = 0.f, inv = 0.f, zp = 0.f;
+    if (row < q.rows && s_src[r] >= 0) {
+      if (R == Q_TENSOR_BIP || R == Q_TENSOR_UNI) {
+        inv = __ldg(q.params + q.param_off);
+        zp = R == Q_TENSOR_UNI ? __ldg(q.params + q.param_off + 2) : 0.f;
+      } else if (R == Q_HEAD_BIP) {
+        inv = __ldg(q.params + row / q.rows_per_batch);
+      } else if (self) {
+        float am = 0.f, mx = -INFINITY, mn = INFINITY;
+        for (int w = 0; w < 8; ++w) {
+          am = fmaxf(am, s_red[0][r][w]);
+          mx = fmaxf(mx, s_red[1][r][w]);
+          mn = fminf(mn, s_red[2][r][w]);
+        }
+        if (R == Q_GROUP_ASYM) {
+          sc = fdiv(fmaxf(fsub(mx, mn), 1e-5f), qf);
+          zp = fclamp(frint(fdiv(-mn, sc)), 0.f, qf);
+        } else {
+          sc = fdiv(fmaxf(am, 1e-5f), qf);
+        }
+      } else {
+        sc = __ldg(q.row_scale + row);
+        if (R == Q_GROUP_ASYM) zp = __ldg(q.row_zp + row);
+      }
+    }
+    s_sc[r] = sc;
+    s_inv[r] = inv;
+    s_zp[r] = zp;
+  }
+  __syncthreads();
+  // quantise: item i is block jb = i / RT of row r = i % RT
+  const int nb = d8(q.d);
+  for (int i = tid; i < RT * nb; i += 256) {
+    const int r = i % RT, jb = i / RT, row = row0 + r;
+    if (row >= q.rows) continue;
+    const int src = s_src[r];
+    const int j0 = 8 * jb;
+    uint32_t packed[4] = {0u, 0u, 0u, 0u};
+    if (src >= 0) {
+      const LevelQ lq = s_lev[r] >= 0 ? q.lq[s_lev[r]] : LevelQ{q.ratio, q.G, q.vcap, q.ktab, q.amap};
+      const float sc = s_sc[r], inv = s_inv[r], zp = s_zp[r];
+      // the block's eight values (the padded row holds 8 * ceil(d / 8) of them)
+      const float4* p4 = reinterpret_cast<const float4*>(xsm + r * stride + j0);
+      const float4 u = p4[0], w = p4[1];
+      float xs[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+      float rsum = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int j = j0 + e;
+        int16_t code = 0;
+        if (j < q.d) {
+          float x = xs[e];
+          if (q.smooth) x = q.smooth_div ? fdiv(x, __ldg(q.smooth + j)) : fmul(x, __ldg(q.smooth + j));
+          code = quant_one<R>(q, lq, j, x, sc, inv, zp, qf, rsum);
+        }
+        packed[e >> 1] |= (uint32_t)(uint16_t)code << (16 * (e & 1));
+      }
+      if (q.row_sum) atomicAdd(&s_sum[r], rsum);
+    }
+    *reinterpret_cast<uint4*>(q.out16 + blk_idx(q.rows, row, j0)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  }
+  __syncthreads();
+  if (tid < RT && row0 + tid < q.rows) {
+    const int r = tid, row = row0 + r;
+    if (self || s_src[r] < 0) {
+      if (q.row_scale) q.row_scale[row] = s_sc[r];
+      if (R == Q_GROUP_ASYM && q.row_zp) q.row_zp[row] = s_zp[r];
+    }
+    if (q.row_sum) q.row_sum[row] = s_sum[r];
+  }
+}
+
+// Rows per block of the staged quantiser for d dimensions (72 KB of shared
+// memory at most), 0 when the rows are too long for it.
+static int tile_rows(int d) {
+  const size_t row_bytes = (size_t)(4 * ((d + 3) / 4) + 4) * sizeof(float);
+  for (int rt = 4; rt >= 1; rt >>= 1)
+    if (rt * row_bytes <= (72u << 10)) return rt;
+  return 0;
+}
+
+template <int R, int RT>
+static cudaError_t launch_tile(const QuantArgs& q, cudaStream_t st) {
+  const size_t smem = (size_t)RT * (4 * ((q.d + 3) / 4) + 4) * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(quant_tile_kernel<R, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  quant_tile_kernel<R, RT><<<cdiv(q.rows, RT), 256, smem, st>>>(q);
+  count_launch();
+  return cudaGetLastError();
+}
+
+template <int R>
+static cudaError_t launch_tile_rt(const QuantArgs& q, cudaStream_t st) {
+  switch (tile_rows(q.d)) {
+    case 4: return launch_tile<R, 4>(q, st);
+    case 2: return launch_tile<R, 2>(q, st);
+    default: return launch_tile<R, 1>(q, st);
   }
 }
 
@@ -487,6 +712,22 @@ cudaError_t launch_tensor_params(const float* sa, int ra, const float* sb, int r
 
 cudaError_t launch_quant_rows(int recipe, const QuantArgs& q, cudaStream_t st) {
   if (q.rows <= 0) return cudaSuccess;
+  // SCMP_QUANT_STAGED=1 in the environment: the staged kernel for every recipe
+  // but the chunked one, while rows fit its shared memory (measured slower
+  // than one warp per row: config 5 2.49 against 1.13 ms, config 2 0.29
+  // against 0.25 ms)
+  const char* es = getenv("SCMP_QUANT_STAGED");
+  if (recipe != Q_ROWCHUNK_BIP && tile_rows(q.d) > 0 && es && es[0] == '1') {
+    switch (recipe) {
+      case Q_TENSOR_BIP: return launch_tile_rt<Q_TENSOR_BIP>(q, st);
+      case Q_TENSOR_UNI: return launch_tile_rt<Q_TENSOR_UNI>(q, st);
+      case Q_GROUP_SYM: return launch_tile_rt<Q_GROUP_SYM>(q, st);
+      case Q_GROUP_ASYM: return launch_tile_rt<Q_GROUP_ASYM>(q, st);
+      case Q_BATCH_SYM: return launch_tile_rt<Q_BATCH_SYM>(q, st);
+      case Q_HEAD_BIP: return launch_tile_rt<Q_HEAD_BIP>(q, st);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   const dim3 g = warp_grid(q.rows);
   switch (recipe) {
     case Q_TENSOR_BIP: { quant_rows_kernel<Q_TENSOR_BIP><<<g, 256, 0, st>>>(q); count_launch(); } break;

@@ -147,7 +147,7 @@ def _fused(a, shape, offset: int, ld: int, group, compute, copy: bool = True):
     if po is None:
         po = _PEER_OUTPUTS[key] = _PeerOutputs(shape, a.device, group)
     view, ptrs = po.take()
-    with K.output_to(ptrs, offset, ld, view):
+    with K.output_to(ptrs, offset, ld, view, self_index=po.rank):
         compute()
     # every rank's epilogue has stored its block once this collective completes
     dist.all_reduce(torch.zeros(1, device=a.device), group=group)

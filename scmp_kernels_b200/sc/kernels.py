@@ -261,15 +261,21 @@ _REDIRECT = threading.local()
 
 
 @contextlib.contextmanager
-def output_to(peers, offset: int, ld: int, result: torch.Tensor):
+def output_to(peers, offset: int, ld: int, result: torch.Tensor, self_index: int = -1):
     """Within the block, every sc_matmul launch of this thread stores its
     (batch, n, m) result at element ``offset + (h*n + i)*ld + j`` of each device
     pointer in ``peers`` (the multi-GPU all-gather fused into the GEMM's
-    epilogue) and returns ``result`` instead of a new tensor."""
+    epilogue) and returns ``result`` instead of a new tensor. ``self_index``:
+    the entry of ``peers`` in this device's memory, if any (the GEMM then
+    stores each tile there first and copies it to the others while the next
+    tile computes)."""
     if not 1 <= len(peers) <= _lib.MAX_OUT_PEERS:
         raise ValueError(f"output_to: 1..{_lib.MAX_OUT_PEERS} destinations, got {len(peers)}")
+    if not -1 <= self_index < len(peers):
+        raise ValueError(f"output_to: self_index {self_index} outside the destinations")
     prev = getattr(_REDIRECT, "value", None)
-    _REDIRECT.value = ((ctypes.c_void_p * len(peers))(*peers), len(peers), int(offset), int(ld), result)
+    _REDIRECT.value = ((ctypes.c_void_p * len(peers))(*peers), len(peers), int(offset), int(ld), result,
+                       int(self_index))
     try:
         yield
     finally:
@@ -308,7 +314,7 @@ def _launch(gran: int, mode: str, a: torch.Tensor, b: torch.Tensor, sc_prec: int
     dev = a.device
     redirect = getattr(_REDIRECT, "value", None)
     if redirect is not None:
-        peers, n_peers, out_offset, out_ld, out = redirect
+        peers, n_peers, out_offset, out_ld, out, self_index = redirect
     elif out is None:
         out = torch.empty((batch, n, m) if three_d else (n, m), dtype=torch.float32, device=dev)
     amap, bmap = tables.maps_for(d, period)
@@ -326,6 +332,7 @@ def _launch(gran: int, mode: str, a: torch.Tensor, b: torch.Tensor, sc_prec: int
         desc.out = None
         desc.out_peers = ctypes.cast(peers, ctypes.c_void_p)
         desc.n_out_peers, desc.out_offset, desc.out_ld = n_peers, out_offset, out_ld
+        desc.out_self = self_index + 1
     L = _lib.lib()
     ws_bytes = ctypes.c_size_t(0)
     _lib.check(L.scmp_sc_matmul_workspace_size(ctypes.byref(desc), ctypes.byref(ws_bytes)), "sc_matmul")

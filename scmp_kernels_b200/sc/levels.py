@@ -111,7 +111,7 @@ def sc_matmul_levels(a: torch.Tensor, b: torch.Tensor, row_levels: torch.Tensor,
     redirect = getattr(K._REDIRECT, "value", None)
     out = None
     if redirect is not None:
-        peers, n_peers, out_offset, out_ld, out = redirect
+        peers, n_peers, out_offset, out_ld, out, self_index = redirect
     else:
         out = torch.empty((n, m), dtype=torch.float32, device=dev)
     desc = _lib.MatmulDesc(
@@ -123,6 +123,7 @@ def sc_matmul_levels(a: torch.Tensor, b: torch.Tensor, row_levels: torch.Tensor,
         desc.out = None
         desc.out_peers = ctypes.cast(peers, ctypes.c_void_p)
         desc.n_out_peers, desc.out_offset, desc.out_ld = n_peers, out_offset, out_ld
+        desc.out_self = self_index + 1
     L_ = _lib.lib()
     ws_bytes = ctypes.c_size_t(0)
     _lib.check(L_.scmp_sc_matmul_levels_workspace_size(ctypes.byref(desc), levels, nlev, ctypes.byref(ws_bytes)),

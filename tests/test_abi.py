@@ -23,7 +23,7 @@ def declared_functions():
 def test_library_builds_and_loads():
     from scmp_kernels_b200 import build
     build.build()
-    assert _lib.load().scmp_abi_version() == _lib.ABI_VERSION == 3
+    assert _lib.load().scmp_abi_version() == _lib.ABI_VERSION == 4
 
 
 def test_every_declared_symbol_is_exported():

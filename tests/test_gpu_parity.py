@@ -222,6 +222,39 @@ def test_band_grouped_tile_order_matches_default(shape, kw, group, monkeypatch, 
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("shape,kw", [
+    ((300, 520, 4096), dict(granularity="per_row", sc_prec=8)),                          # 4 rows per block
+    ((129, 77, 8192), dict(granularity="per_row", mode="unipolar", sc_prec=6, stoc_len=64, smooth=True)),
+    ((70, 90, 301), dict(granularity="per_row", sc_prec=8, group_a=3, group_b=7)),      # ragged d: scalar loads
+    ((50, 60, 16400), dict(granularity="per_row", sc_prec=8)),                          # one row per block
+    ((20000 // 100, 40, 20000), dict(granularity="per_row", sc_prec=7)),                # too long: warp kernel
+    ((33, 90, 130), dict(granularity="per_tensor", mode="unipolar", sc_prec=7)),
+    ((3, 40, 50, 64), dict(granularity="per_head", sc_prec=8)),
+    ((2, 9, 140, 31), dict(granularity="per_row", sc_prec=8)),                           # 3D per_row
+])
+def test_staged_quantiser_matches_warp_quantiser(shape, kw, monkeypatch, env_vars):
+    """The staged quantiser (rows in shared memory, one pass;
+    SCMP_QUANT_STAGED=1) and the default warp-per-row one give the same bits."""
+    env_vars({})
+    kw = dict(kw)
+    g = torch.Generator(device=DEV).manual_seed(12)
+    if len(shape) == 4:
+        bh, n, m, d = shape
+        a, b = torch.randn(bh, n, d, device=DEV, generator=g), torch.randn(bh, m, d, device=DEV, generator=g)
+    else:
+        n, m, d = shape
+        a, b = torch.randn(n, d, device=DEV, generator=g), torch.randn(m, d, device=DEV, generator=g) * 0.05
+    if kw.pop("smooth", False):
+        kw["smooth_scales"] = torch.rand(a.shape[-1], device=DEV, generator=g) + 0.5
+    monkeypatch.setattr(K, "_FORCE_SIMT", False)
+    monkeypatch.setenv("SCMP_QUANT_STAGED", "1")
+    y_staged = sc_matmul(a, b, **kw)
+    monkeypatch.setenv("SCMP_QUANT_STAGED", "0")
+    y_warp = sc_matmul(a, b, **kw)
+    assert torch.equal(y_staged, y_warp)
+    assert _lib.device_error() == 0
+
+
 @pytest.mark.parametrize("gran,shape", [("per_row", (70, 300, 500)), ("per_tensor", (33, 90, 130)),
                                         ("per_head", (3, 40, 50, 64))])
 @pytest.mark.parametrize("simt", [False, True])
@@ -388,6 +421,30 @@ def test_cpu_inputs_round_trip_and_device_guard():
     assert torch.cuda.current_device() == 0
     y2 = sc_matmul(a.cuda(), b.cuda(), "per_row")
     assert torch.equal(y, y2.cpu())
+
+
+@pytest.mark.parametrize("shape,self_index", [((4096, 3000, 640), 1), ((600, 1700, 1000), 0), ((300, 520, 700), 2)])
+def test_deferred_peer_copies_fill_every_buffer(shape, self_index, env_vars):
+    """With one destination marked as this device's own, the wide-tile GEMM
+    stores each whole tile there and its epilogue warps copy it to the other
+    destinations while the next tile computes (tail pieces store to all
+    directly): every buffer gets the result at its offset and row stride."""
+    env_vars({})
+    n, m, d = shape
+    g = torch.Generator(device=DEV).manual_seed(19)
+    a, b = torch.randn(n, d, device=DEV, generator=g), torch.randn(m, d, device=DEV, generator=g) * 0.05
+    ref = sc_matmul(a, b, "per_row", sc_prec=8)
+    # one case with 16-byte-aligned rows (whole-vector copies), the others not
+    ld, off = (m + 4, 8) if self_index == 0 else (m + 13, 7)
+    bufs = [torch.full((off + n * ld + 3,), float("nan"), device=DEV) for _ in range(3)]
+    with K.output_to([x.data_ptr() for x in bufs], off, ld, bufs[0], self_index=self_index):
+        sc_matmul(a, b, "per_row", sc_prec=8)
+    torch.cuda.synchronize()
+    for x in bufs:
+        blk = x[off:off + n * ld].view(n, ld)
+        assert torch.equal(blk[:, :m], ref)
+        assert torch.isnan(blk[:, m:]).all() and torch.isnan(x[:off]).all()
+    assert _lib.device_error() == 0
 
 
 @pytest.mark.parametrize("kw", [
