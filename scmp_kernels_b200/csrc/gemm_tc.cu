@@ -1045,7 +1045,8 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
         if (warp == C::EPI_WARP0 && lane == 0)
           *split_flag = atomicAdd(g.split_cnt + st * C::NCTA + rank, 1) == u_last - u_first;
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (*split_flag) {
+        const bool tile_done = *split_flag;  // read once: the next item's piece may overwrite it
+        if (tile_done) {
           // last part to finish: the other parts' accumulators are complete
           __threadfence();
 #pragma unroll 1
@@ -1083,12 +1084,24 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
                         : 0u;
               }
             }
-            store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, m_end, fin, lane);
+            store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, m_end, fin, lane, deferred ? g.out_self - 1 : -1);
+          }
+          if (deferred) {  // this warp's rows of the tile are in this device's destination
+            __threadfence_block();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(cpy_bar);
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar(buf), rank);
+        if (deferred && tile_done) {  // as for whole tiles below: peers' copies under later MMAs
+          if (q != 0) {
+            if (!mbar_wait(cpy_bar, cpy_phase & 1, abort_flag, 8)) goto epi_out;
+            copy_rows_to_peers(g, g.out_self - 1, bh, a0 + (int)rank * C::BM, C::BM, b0, m_end, q - 1, 3, lane);
+          }
+          ++cpy_phase;
+        }
         continue;
       }
       const bool chunked = ep.kind == EPI_CHUNK;

@@ -419,196 +419,179 @@ __global__ void quant_rows_kernel(QuantArgs q) {
 }
 
 // --------------------------------------------------------------------------
-// quantisers, staged: RT rows per block of 256 threads, one pass over HBM
+// quantisers: one block of 256 threads per row, the row held in registers
 // --------------------------------------------------------------------------
 
-// The non-chunked recipes of quant_rows_kernel with RT consecutive rows per
-// block: the rows are copied to shared memory with cp.async (16-byte copies,
-// all in flight at once; rows of a misaligned or ragged x are loaded element
-// by element), the row statistics are reduced from shared memory, and the
-// operand is written one block of eight dimensions for each of the RT rows at
-// a time, so that each store instruction fills RT * 16 contiguous bytes of the
-// blocked layout. Smoothing is applied where the values are read. Results are
-// identical to quant_rows_kernel (same per-element recipe, and the row sums
-// add exact integers, in any order).
-template <int R, int RT>
-__global__ void __launch_bounds__(256) quant_tile_kernel(QuantArgs q) {
-  extern __shared__ __align__(16) float xsm[];  // RT rows, stride elements each
-  __shared__ float s_sc[RT], s_inv[RT], s_zp[RT], s_sum[RT];
-  __shared__ int s_src[RT], s_lev[RT];
-  __shared__ float s_red[3][RT][8];
+// The non-chunked recipes of quant_rows_kernel with one row per block: each
+// thread loads its NB blocks of eight dimensions (blocks t, t + 256, ...; two
+// 16-byte loads each, all in flight at once), smooths them once, reduces the
+// row statistics over the block and quantises from its registers. One pass
+// over HBM, the smoothing division done once per element. Results are
+// identical to quant_rows_kernel (same per-element recipe; the row sums add
+// exact integers, so their order does not matter).
+template <int R, int NB>
+__global__ void __launch_bounds__(256) quant_row_cta_kernel(QuantArgs q) {
+  __shared__ int s_bnd[kBndTab];
+  __shared__ float s_red[3][8];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int row0 = blockIdx.x * RT;
-  const int d4 = (q.d + 3) >> 2;
-  const int stride = 4 * d4 + 4;  // floats; 16 bytes of padding between rows
+  const int row = blockIdx.x;
   const float qf = (float)q.q;
-  if (tid < RT) {
-    const int row = row0 + tid;
-    int src = row < q.rows ? row : -1;
-    int lv = -1;
-    if (q.row_of && src >= 0) {
-      src = __ldg(q.row_of + row);
-      lv = q.nlev - 1;
-      for (int l = 0; l < q.nlev; ++l)
-        if ((row >> 8) < __ldg(q.lev_tile0 + l + 1)) {
-          lv = l;
-          break;
-        }
-    }
-    s_src[tid] = src;
-    s_lev[tid] = lv;
-    s_sum[tid] = 0.f;
-  }
-  __syncthreads();
-  // stage the rows
-  const bool async = q.vec != 0;
-#pragma unroll
-  for (int r = 0; r < RT; ++r) {
-    const int src = s_src[r];
-    float* dst = xsm + r * stride;
-    if (src < 0) continue;
-    if (async) {
-      const float* gsrc = q.x + (size_t)src * q.d;
-      for (int c = tid; c < d4; c += 256) {
-        const uint32_t sa = smem_u32(dst + 4 * c);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gsrc + 4 * c) : "memory");
+  int src = row;
+  LevelQ lq{q.ratio, q.G, q.vcap, q.ktab, q.amap};
+  if (q.row_of) {
+    src = __ldg(q.row_of + row);
+    int lv = q.nlev - 1;
+    for (int l = 0; l < q.nlev; ++l)
+      if ((row >> 8) < __ldg(q.lev_tile0 + l + 1)) {
+        lv = l;
+        break;
       }
+    lq = q.lq[lv];
+  }
+  const bool use_tab = q.q + 1 < kBndTab;
+  if (use_tab)
+    for (int i = tid; i <= q.q + 1; i += 256) s_bnd[i] = bnd_of<R>(lq, (float)i, qf);
+  const int nb = d8(q.d);
+  int16_t* out = q.out16;
+  if (src < 0) {  // padding row of a level's last tile: a zero operand
+    for (int jb = tid; jb < nb; jb += 256)
+      *reinterpret_cast<uint4*>(out + blk_idx(q.rows, row, 8 * jb)) = make_uint4(0, 0, 0, 0);
+    if (tid == 0) {
+      if (q.row_scale) q.row_scale[row] = 0.f;
+      if (q.row_zp) q.row_zp[row] = 0.f;
+      if (q.row_sum) q.row_sum[row] = 0.f;
+    }
+    return;  // uniform over the block: no barrier follows for it
+  }
+  float xs[NB][8];
+#pragma unroll
+  for (int k = 0; k < NB; ++k) {
+    const int j0 = 8 * (tid + 256 * k);
+    if (q.vec && j0 + 8 <= q.d) {
+      const float4* sp = reinterpret_cast<const float4*>(q.x + (size_t)src * q.d + j0);
+      const float4 u = __ldg(sp), w = __ldg(sp + 1);
+      xs[k][0] = u.x; xs[k][1] = u.y; xs[k][2] = u.z; xs[k][3] = u.w;
+      xs[k][4] = w.x; xs[k][5] = w.y; xs[k][6] = w.z; xs[k][7] = w.w;
     } else {
-      for (int j = tid; j < q.d; j += 256) dst[j] = __ldg(q.x + (size_t)src * q.d + j);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xs[k][e] = j0 + e < q.d ? __ldg(q.x + (size_t)src * q.d + j0 + e) : 0.f;
     }
   }
-  if (async) asm volatile("cp.async.wait_all;" ::: "memory");
-  __syncthreads();
-  auto xval = [&](int r, int j) -> float {  // smoothed element j of staged row r
-    float x = xsm[r * stride + j];
-    if (q.smooth) x = q.smooth_div ? fdiv(x, __ldg(q.smooth + j)) : fmul(x, __ldg(q.smooth + j));
-    return x;
-  };
-  // per-row parameters
-  const bool self = (R == Q_GROUP_SYM || R == Q_GROUP_ASYM || R == Q_BATCH_SYM) && q.self_stats;
-  if (self) {
+  if (q.smooth) {
 #pragma unroll
-    for (int r = 0; r < RT; ++r) {
-      float am = 0.f, mx = -INFINITY, mn = INFINITY;
-      if (s_src[r] >= 0)
-        for (int j = tid; j < q.d; j += 256) {
-          const float x = xval(r, j);
+    for (int k = 0; k < NB; ++k)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int j = 8 * (tid + 256 * k) + e;
+        if (j < q.d) {
+          const float sv = __ldg(q.smooth + j);
+          xs[k][e] = q.smooth_div ? fdiv(xs[k][e], sv) : fmul(xs[k][e], sv);
+        }
+      }
+  }
+  const bool self = (R == Q_GROUP_SYM || R == Q_GROUP_ASYM || R == Q_BATCH_SYM) && q.self_stats;
+  float sc = 0.f, inv = 0.f, zp = 0.f;
+  if (self) {
+    float am = 0.f, mx = -INFINITY, mn = INFINITY;
+#pragma unroll
+    for (int k = 0; k < NB; ++k)
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (8 * (tid + 256 * k) + e < q.d) {
+          const float x = xs[k][e];
           am = fmaxf(am, fabsf(x));
           mx = fmaxf(mx, x);
           mn = fminf(mn, x);
         }
-      am = warp_max(am);
-      mx = warp_max(mx);
-      mn = warp_min(mn);
-      if (lane == 0) {
-        s_red[0][r][warp] = am;
-        s_red[1][r][warp] = mx;
-        s_red[2][r][warp] = mn;
-      }
+    am = warp_max(am);
+    mx = warp_max(mx);
+    mn = warp_min(mn);
+    if (lane == 0) {
+      s_red[0][warp] = am;
+      s_red[1][warp] = mx;
+      s_red[2][warp] = mn;
     }
     __syncthreads();
-  }
-  if (tid < RT) {
-    const int r = tid, row = row0 + r;
-    float sc = 0.f, inv = 0.f, zp = 0.f;
-    if (row < q.rows && s_src[r] >= 0) {
-      if (R == Q_TENSOR_BIP || R == Q_TENSOR_UNI) {
-        inv = __ldg(q.params + q.param_off);
-        zp = R == Q_TENSOR_UNI ? __ldg(q.params + q.param_off + 2) : 0.f;
-      } else if (R == Q_HEAD_BIP) {
-        inv = __ldg(q.params + row / q.rows_per_batch);
-      } else if (self) {
-        float am = 0.f, mx = -INFINITY, mn = INFINITY;
-        for (int w = 0; w < 8; ++w) {
-          am = fmaxf(am, s_red[0][r][w]);
-          mx = fmaxf(mx, s_red[1][r][w]);
-          mn = fminf(mn, s_red[2][r][w]);
-        }
-        if (R == Q_GROUP_ASYM) {
-          sc = fdiv(fmaxf(fsub(mx, mn), 1e-5f), qf);
-          zp = fclamp(frint(fdiv(-mn, sc)), 0.f, qf);
-        } else {
-          sc = fdiv(fmaxf(am, 1e-5f), qf);
-        }
-      } else {
-        sc = __ldg(q.row_scale + row);
-        if (R == Q_GROUP_ASYM) zp = __ldg(q.row_zp + row);
-      }
+    am = s_red[0][0];
+    mx = s_red[1][0];
+    mn = s_red[2][0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) {
+      am = fmaxf(am, s_red[0][w]);
+      mx = fmaxf(mx, s_red[1][w]);
+      mn = fminf(mn, s_red[2][w]);
     }
-    s_sc[r] = sc;
-    s_inv[r] = inv;
-    s_zp[r] = zp;
+    if (R == Q_GROUP_ASYM) {
+      sc = fdiv(fmaxf(fsub(mx, mn), 1e-5f), qf);
+      zp = fclamp(frint(fdiv(-mn, sc)), 0.f, qf);
+    } else {
+      sc = fdiv(fmaxf(am, 1e-5f), qf);
+    }
+    if (tid == 0) {
+      q.row_scale[row] = sc;
+      if (R == Q_GROUP_ASYM) q.row_zp[row] = zp;
+    }
+  } else {
+    __syncthreads();  // the boundary table is complete
+    if (R == Q_TENSOR_BIP || R == Q_TENSOR_UNI) {
+      inv = __ldg(q.params + q.param_off);
+      zp = R == Q_TENSOR_UNI ? __ldg(q.params + q.param_off + 2) : 0.f;
+    } else if (R == Q_HEAD_BIP) {
+      inv = __ldg(q.params + row / q.rows_per_batch);
+    } else {
+      sc = __ldg(q.row_scale + row);
+      if (R == Q_GROUP_ASYM) zp = __ldg(q.row_zp + row);
+    }
   }
-  __syncthreads();
-  // quantise: item i is block jb = i / RT of row r = i % RT
-  const int nb = d8(q.d);
-  for (int i = tid; i < RT * nb; i += 256) {
-    const int r = i % RT, jb = i / RT, row = row0 + r;
-    if (row >= q.rows) continue;
-    const int src = s_src[r];
+  const int* tab = use_tab ? s_bnd : nullptr;
+  float rsum = 0.f;
+#pragma unroll
+  for (int k = 0; k < NB; ++k) {
+    const int jb = tid + 256 * k;
+    if (jb >= nb) break;
     const int j0 = 8 * jb;
     uint32_t packed[4] = {0u, 0u, 0u, 0u};
-    if (src >= 0) {
-      const LevelQ lq = s_lev[r] >= 0 ? q.lq[s_lev[r]] : LevelQ{q.ratio, q.G, q.vcap, q.ktab, q.amap};
-      const float sc = s_sc[r], inv = s_inv[r], zp = s_zp[r];
-      // the block's eight values (the padded row holds 8 * ceil(d / 8) of them)
-      const float4* p4 = reinterpret_cast<const float4*>(xsm + r * stride + j0);
-      const float4 u = p4[0], w = p4[1];
-      float xs[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
-      float rsum = 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int j = j0 + e;
-        int16_t code = 0;
-        if (j < q.d) {
-          float x = xs[e];
-          if (q.smooth) x = q.smooth_div ? fdiv(x, __ldg(q.smooth + j)) : fmul(x, __ldg(q.smooth + j));
-          code = quant_one<R>(q, lq, j, x, sc, inv, zp, qf, rsum);
-        }
-        packed[e >> 1] |= (uint32_t)(uint16_t)code << (16 * (e & 1));
-      }
-      if (q.row_sum) atomicAdd(&s_sum[r], rsum);
+    for (int e = 0; e < 8; ++e) {
+      const int j = j0 + e;
+      int16_t code = 0;
+      if (j < q.d) code = quant_one<R>(q, lq, j, xs[k][e], sc, inv, zp, qf, rsum, tab);
+      packed[e >> 1] |= (uint32_t)(uint16_t)code << (16 * (e & 1));
     }
-    *reinterpret_cast<uint4*>(q.out16 + blk_idx(q.rows, row, j0)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    *reinterpret_cast<uint4*>(out + blk_idx(q.rows, row, j0)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
   }
-  __syncthreads();
-  if (tid < RT && row0 + tid < q.rows) {
-    const int r = tid, row = row0 + r;
-    if (self || s_src[r] < 0) {
-      if (q.row_scale) q.row_scale[row] = s_sc[r];
-      if (R == Q_GROUP_ASYM && q.row_zp) q.row_zp[row] = s_zp[r];
+  if (q.row_sum) {
+    rsum = warp_sum(rsum);
+    __syncthreads();  // every thread has read s_red
+    if (lane == 0) s_red[0][warp] = rsum;
+    __syncthreads();
+    if (tid == 0) {
+      float t = 0.f;
+      for (int w = 0; w < 8; ++w) t = fadd(t, s_red[0][w]);
+      q.row_sum[row] = t;
     }
-    if (q.row_sum) q.row_sum[row] = s_sum[r];
   }
 }
 
-// Rows per block of the staged quantiser for d dimensions (72 KB of shared
-// memory at most), 0 when the rows are too long for it.
-static int tile_rows(int d) {
-  const size_t row_bytes = (size_t)(4 * ((d + 3) / 4) + 4) * sizeof(float);
-  for (int rt = 4; rt >= 1; rt >>= 1)
-    if (rt * row_bytes <= (72u << 10)) return rt;
+// Blocks of eight dimensions per thread of quant_row_cta_kernel for d (0:
+// rows too long, quant_rows_kernel instead).
+static int row_cta_blocks(int d) {
+  const int nb = d8(d);
+  for (int k = 1; k <= 8; k *= 2)
+    if (nb <= 256 * k) return k;
   return 0;
 }
 
-template <int R, int RT>
-static cudaError_t launch_tile(const QuantArgs& q, cudaStream_t st) {
-  const size_t smem = (size_t)RT * (4 * ((q.d + 3) / 4) + 4) * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(quant_tile_kernel<R, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-  if (e != cudaSuccess) return e;
-  quant_tile_kernel<R, RT><<<cdiv(q.rows, RT), 256, smem, st>>>(q);
+template <int R>
+static cudaError_t launch_row_cta(const QuantArgs& q, cudaStream_t st) {
+  switch (row_cta_blocks(q.d)) {
+    case 1: quant_row_cta_kernel<R, 1><<<q.rows, 256, 0, st>>>(q); break;
+    case 2: quant_row_cta_kernel<R, 2><<<q.rows, 256, 0, st>>>(q); break;
+    case 4: quant_row_cta_kernel<R, 4><<<q.rows, 256, 0, st>>>(q); break;
+    default: quant_row_cta_kernel<R, 8><<<q.rows, 256, 0, st>>>(q); break;
+  }
   count_launch();
   return cudaGetLastError();
-}
-
-template <int R>
-static cudaError_t launch_tile_rt(const QuantArgs& q, cudaStream_t st) {
-  switch (tile_rows(q.d)) {
-    case 4: return launch_tile<R, 4>(q, st);
-    case 2: return launch_tile<R, 2>(q, st);
-    default: return launch_tile<R, 1>(q, st);
-  }
 }
 
 // --------------------------------------------------------------------------
@@ -712,19 +695,17 @@ cudaError_t launch_tensor_params(const float* sa, int ra, const float* sb, int r
 
 cudaError_t launch_quant_rows(int recipe, const QuantArgs& q, cudaStream_t st) {
   if (q.rows <= 0) return cudaSuccess;
-  // SCMP_QUANT_STAGED=1 in the environment: the staged kernel for every recipe
-  // but the chunked one, while rows fit its shared memory (measured slower
-  // than one warp per row: config 5 2.49 against 1.13 ms, config 2 0.29
-  // against 0.25 ms)
-  const char* es = getenv("SCMP_QUANT_STAGED");
-  if (recipe != Q_ROWCHUNK_BIP && tile_rows(q.d) > 0 && es && es[0] == '1') {
+  // one block per row for every recipe but the chunked one, while a row fits
+  // its registers (SCMP_QUANT_WARP=1 in the environment: one warp per row)
+  const char* ew = getenv("SCMP_QUANT_WARP");
+  if (recipe != Q_ROWCHUNK_BIP && row_cta_blocks(q.d) > 0 && !(ew && ew[0] == '1')) {
     switch (recipe) {
-      case Q_TENSOR_BIP: return launch_tile_rt<Q_TENSOR_BIP>(q, st);
-      case Q_TENSOR_UNI: return launch_tile_rt<Q_TENSOR_UNI>(q, st);
-      case Q_GROUP_SYM: return launch_tile_rt<Q_GROUP_SYM>(q, st);
-      case Q_GROUP_ASYM: return launch_tile_rt<Q_GROUP_ASYM>(q, st);
-      case Q_BATCH_SYM: return launch_tile_rt<Q_BATCH_SYM>(q, st);
-      case Q_HEAD_BIP: return launch_tile_rt<Q_HEAD_BIP>(q, st);
+      case Q_TENSOR_BIP: return launch_row_cta<Q_TENSOR_BIP>(q, st);
+      case Q_TENSOR_UNI: return launch_row_cta<Q_TENSOR_UNI>(q, st);
+      case Q_GROUP_SYM: return launch_row_cta<Q_GROUP_SYM>(q, st);
+      case Q_GROUP_ASYM: return launch_row_cta<Q_GROUP_ASYM>(q, st);
+      case Q_BATCH_SYM: return launch_row_cta<Q_BATCH_SYM>(q, st);
+      case Q_HEAD_BIP: return launch_row_cta<Q_HEAD_BIP>(q, st);
       default: return cudaErrorInvalidValue;
     }
   }

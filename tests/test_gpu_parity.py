@@ -223,18 +223,19 @@ def test_band_grouped_tile_order_matches_default(shape, kw, group, monkeypatch, 
 
 
 @pytest.mark.parametrize("shape,kw", [
-    ((300, 520, 4096), dict(granularity="per_row", sc_prec=8)),                          # 4 rows per block
+    ((300, 520, 4096), dict(granularity="per_row", sc_prec=8)),                          # 2 blocks per thread
     ((129, 77, 8192), dict(granularity="per_row", mode="unipolar", sc_prec=6, stoc_len=64, smooth=True)),
     ((70, 90, 301), dict(granularity="per_row", sc_prec=8, group_a=3, group_b=7)),      # ragged d: scalar loads
-    ((50, 60, 16400), dict(granularity="per_row", sc_prec=8)),                          # one row per block
+    ((50, 60, 16384), dict(granularity="per_row", sc_prec=8)),                          # 8 blocks per thread
     ((20000 // 100, 40, 20000), dict(granularity="per_row", sc_prec=7)),                # too long: warp kernel
+    ((64, 48, 3000), dict(granularity="per_row", sc_prec=10)),                          # q > 256: no table
     ((33, 90, 130), dict(granularity="per_tensor", mode="unipolar", sc_prec=7)),
     ((3, 40, 50, 64), dict(granularity="per_head", sc_prec=8)),
     ((2, 9, 140, 31), dict(granularity="per_row", sc_prec=8)),                           # 3D per_row
 ])
-def test_staged_quantiser_matches_warp_quantiser(shape, kw, monkeypatch, env_vars):
-    """The staged quantiser (rows in shared memory, one pass;
-    SCMP_QUANT_STAGED=1) and the default warp-per-row one give the same bits."""
+def test_row_block_quantiser_matches_warp_quantiser(shape, kw, monkeypatch, env_vars):
+    """The default quantiser (one block per row, the row in registers, one
+    pass) and the warp-per-row one (SCMP_QUANT_WARP=1) give the same bits."""
     env_vars({})
     kw = dict(kw)
     g = torch.Generator(device=DEV).manual_seed(12)
@@ -247,9 +248,9 @@ def test_staged_quantiser_matches_warp_quantiser(shape, kw, monkeypatch, env_var
     if kw.pop("smooth", False):
         kw["smooth_scales"] = torch.rand(a.shape[-1], device=DEV, generator=g) + 0.5
     monkeypatch.setattr(K, "_FORCE_SIMT", False)
-    monkeypatch.setenv("SCMP_QUANT_STAGED", "1")
+    monkeypatch.setenv("SCMP_QUANT_WARP", "0")
     y_staged = sc_matmul(a, b, **kw)
-    monkeypatch.setenv("SCMP_QUANT_STAGED", "0")
+    monkeypatch.setenv("SCMP_QUANT_WARP", "1")
     y_warp = sc_matmul(a, b, **kw)
     assert torch.equal(y_staged, y_warp)
     assert _lib.device_error() == 0
