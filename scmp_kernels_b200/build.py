@@ -44,6 +44,10 @@ def build(force: bool = False, verbose: bool = False) -> str:
         return OUT
     cmd = [_nvcc(), *NVCC_FLAGS, "-I", os.path.join(REPO, "include"), "-o", OUT, MAIN]
     r = subprocess.run(cmd, capture_output=True, text=True)
+    # the compiler's report (ptxas registers, spills, shared memory per kernel)
+    os.makedirs(os.path.join(HERE, "_build"), exist_ok=True)
+    with open(os.path.join(HERE, "_build", "nvcc.log"), "w") as f:
+        f.write(r.stdout + r.stderr)
     if verbose or r.returncode:
         sys.stderr.write(r.stdout + r.stderr)
     if r.returncode:

@@ -611,12 +611,38 @@ __device__ __forceinline__ bool produce_item(const GemmArgs& g, const Sched& sc,
         bm_hi = __ldg(bmsrc + 2 * blk0 + 1);
         load_stream_words<TLEN, SPD, F4>(bs.vcap1, bs.pat, kv_cur, bm_lo, bm_hi, 0, d0, d1, valid, LW, pw);
       }
+      // Blocks of one stage (64-long e2m1 streams): the next block's operand
+      // values (and table rows) are loaded two blocks ahead, so that a whole
+      // stage hides their latency; longer blocks load one block ahead.
+      uint4 kv_ahead = make_uint4(0, 0, 0, 0);
+      int4 ab_lo = make_int4(0, 0, 0, 0), ab_hi = make_int4(0, 0, 0, 0);
+      if constexpr (NSPB == 1) {
+        if (nblk > 1) {
+          if (valid) kv_ahead = __ldg(kvsrc + (size_t)(blk0 + 1) * R + grow);
+          if (!SIDE_A) {
+            ab_lo = __ldg(bmsrc + 2 * (blk0 + 1));
+            ab_hi = __ldg(bmsrc + 2 * (blk0 + 1) + 1);
+          }
+        }
+      }
       for (int blk = 0; blk < nblk; ++blk) {
         const int dbase = d0 + 8 * blk;
         const bool more = blk + 1 < nblk;
         uint4 kv_nxt = make_uint4(0, 0, 0, 0);
         int4 nb_lo = make_int4(0, 0, 0, 0), nb_hi = make_int4(0, 0, 0, 0);
-        if (more) {
+        if constexpr (NSPB == 1) {
+          kv_nxt = kv_ahead;  // block blk + 1 (zeros past the last)
+          nb_lo = ab_lo;
+          nb_hi = ab_hi;
+          kv_ahead = make_uint4(0, 0, 0, 0);
+          if (blk + 2 < nblk) {
+            if (valid) kv_ahead = __ldg(kvsrc + (size_t)(blk0 + blk + 2) * R + grow);
+            if (!SIDE_A) {
+              ab_lo = __ldg(bmsrc + 2 * (blk0 + blk + 2));
+              ab_hi = __ldg(bmsrc + 2 * (blk0 + blk + 2) + 1);
+            }
+          }
+        } else if (more) {
           if (valid) kv_nxt = __ldg(kvsrc + (size_t)(blk0 + blk + 1) * R + grow);
           if (!SIDE_A) {
             nb_lo = __ldg(bmsrc + 2 * (blk0 + blk + 1));
