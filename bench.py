@@ -49,11 +49,9 @@ WORKLOADS = {
     "config4": "per_row bipolar chunk_d=64 ViT-B fc2: a 12608x3072, b 768x3072, p=8, L=256/128/64 by row-range tercile",
 }
 
-# DRAM bytes of one GEMM launch (DRAM read + write bytes) from an ncu capture of
-# the 2048-row case of the config-2 recipe (395.7 MB), scaled to the 4096 rows
-# of the full workload: the a rows, the output and the bands of a that re-read
-# b all double.
-GEMM_TRAFFIC_BYTES = {"config2": 2 * 395.7e6}
+# DRAM bytes (read + write) of one GEMM launch of the full workload on one
+# GPU, from a one-pass ncu capture (dram__bytes_read.sum + dram__bytes_write.sum)
+GEMM_TRAFFIC_BYTES = {"config2": 314.885376e6 + 200.790272e6, "config5": 3151.572736e6 + 971.502592e6}
 
 # Dense tensor-core multiply-accumulates per SM and clock on B200, by operand
 # type (bf16 4096, int8 8192, e2m1 16384), for the fraction of the nominal

@@ -1110,24 +1110,14 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
                         : 0u;
               }
             }
-            store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, m_end, fin, lane, deferred ? g.out_self - 1 : -1);
-          }
-          if (deferred) {  // this warp's rows of the tile are in this device's destination
-            __threadfence_block();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(cpy_bar);
+            // tail tiles end together at the end of the kernel: their stores go
+            // to every destination at once (deferring them measured slower)
+            store_rows32(g, stg, bh, ia - lane, b0 + 32 * cp, m_end, fin, lane);
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar(buf), rank);
-        if (deferred && tile_done) {  // as for whole tiles below: peers' copies under later MMAs
-          if (q != 0) {
-            if (!mbar_wait(cpy_bar, cpy_phase & 1, abort_flag, 8)) goto epi_out;
-            copy_rows_to_peers(g, g.out_self - 1, bh, a0 + (int)rank * C::BM, C::BM, b0, m_end, q - 1, 3, lane);
-          }
-          ++cpy_phase;
-        }
         continue;
       }
       const bool chunked = ep.kind == EPI_CHUNK;
@@ -1226,6 +1216,8 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
           // leader CTA) goes straight on.
           if (q != 0) {
             if (!mbar_wait(cpy_bar, cpy_phase & 1, abort_flag, 7)) goto epi_out;
+            // (spreading the copy over the next tile with pauses between rows
+            // measured slower at 8 devices than copying at full speed)
             copy_rows_to_peers(g, g.out_self - 1, bh, a0 + (int)rank * C::BM, C::BM, b0, m_end, q - 1, 3, lane);
           }
           ++cpy_phase;
