@@ -356,12 +356,8 @@ int scmp_sc_matmul(const scmp_matmul_desc* d, void* workspace, size_t workspace_
       g.epi.bsum = p.sum_b;
     }
   } else if (d->granularity == SCMP_PER_HEAD) {
-    SCMP_CUDA(launch_row_stats(qa, p.stats_a, st), "per_head stats a");
-    SCMP_CUDA(launch_row_stats(qb, p.stats_b, st), "per_head stats b");
-    SCMP_CUDA(launch_group_params(p.stats_a, d->batch, d->n, d->n, q, GP_HEAD, p.scale_a, p.zp_a, st),
-              "per_head params a");
-    SCMP_CUDA(launch_group_params(p.stats_b, d->batch, d->m, d->m, q, GP_HEAD, p.scale_b, p.zp_b, st),
-              "per_head params b");
+    SCMP_CUDA(launch_head_params(qa, d->batch, q, p.scale_a, p.zp_a, st), "per_head params a");
+    SCMP_CUDA(launch_head_params(qb, d->batch, q, p.scale_b, p.zp_b, st), "per_head params b");
     qa.params = p.zp_a;
     qb.params = p.zp_b;
     qa.qmin = qb.qmin = -(float)(q + 1);

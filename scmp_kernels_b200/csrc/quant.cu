@@ -167,6 +167,64 @@ __global__ void group_params_kernel(const float* __restrict__ stats, int rpb, in
   }
 }
 
+// Per-head parameters in one pass (the GP_HEAD recipe of group_params_kernel
+// over row_stats_kernel's statistics, sc/kernels.py:490-495): one block per
+// batch entry reads the entry's
+// rows_per_batch * d (smoothed) values as one contiguous range — 16-byte
+// loads on its aligned middle, several in flight per thread — reduces max and
+// min (order-free, so the bits equal the two-kernel path's, NaN and empty
+// entries included) and writes scale = max(|max|, |min|, 1e-5) / q and its
+// inverse.
+__global__ void __launch_bounds__(512) head_params_kernel(QuantArgs q, int q_max, float* __restrict__ scale,
+                                                          float* __restrict__ inv) {
+  __shared__ float sh[2][16];
+  const size_t n = (size_t)q.rows_per_batch * q.d;
+  const float* x = q.x + (size_t)blockIdx.x * n;
+  float mx = -INFINITY, mn = INFINITY;
+  auto take = [&](size_t i, float v) {
+    if (q.smooth) {
+      const float s = __ldg(q.smooth + (int)(i % (size_t)q.d));
+      v = q.smooth_div ? fdiv(v, s) : fmul(v, s);
+    }
+    mx = fmaxf(mx, v);
+    mn = fminf(mn, v);
+  };
+  // elements before the first 16-byte boundary (x is 4-byte aligned), the
+  // float4 body, the tail
+  const size_t lead = ((16u - (uint32_t)(reinterpret_cast<uintptr_t>(x) & 15u)) & 15u) / 4u;
+  const size_t h0 = lead < n ? lead : n;
+  for (size_t i = threadIdx.x; i < h0; i += blockDim.x) take(i, __ldg(x + i));
+  const size_t n4 = (n - h0) / 4;
+  const float4* x4 = reinterpret_cast<const float4*>(x + h0);
+#pragma unroll 4
+  for (size_t k = threadIdx.x; k < n4; k += blockDim.x) {
+    const float4 v = __ldg(x4 + k);
+    const size_t i = h0 + 4 * k;
+    take(i, v.x);
+    take(i + 1, v.y);
+    take(i + 2, v.z);
+    take(i + 3, v.w);
+  }
+  for (size_t i = h0 + 4 * n4 + threadIdx.x; i < n; i += blockDim.x) take(i, __ldg(x + i));
+  mx = warp_max(mx);
+  mn = warp_min(mn);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    sh[0][w] = mx;
+    sh[1][w] = mn;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < (int)(blockDim.x >> 5); ++k) {
+      mx = fmaxf(mx, sh[0][k]);
+      mn = fminf(mn, sh[1][k]);
+    }
+    const float sc = fdiv(fmaxf(fmaxf(fabsf(mx), fabsf(mn)), 1e-5f), (float)q_max);
+    scale[blockIdx.x] = sc;
+    inv[blockIdx.x] = fdiv(1.0f, sc);
+  }
+}
+
 // Per-tensor parameters for both operands, computed in double like the
 // reference's host code (kernels.py:1173-1186, quant/fused.py:172-174, 204-209,
 // and the scale product of kernels.py:1204). One block of 1024 threads.
@@ -422,27 +480,37 @@ __global__ void quant_rows_kernel(QuantArgs q) {
 // quantisers: one block of 256 threads per row, the row held in registers
 // --------------------------------------------------------------------------
 
-// The non-chunked recipes of quant_rows_kernel with one row per block: each
-// thread loads its NB blocks of eight dimensions (blocks t, t + 256, ...; two
+// The non-chunked recipes of quant_rows_kernel, a row per TPR threads: each
+// thread loads its NB blocks of eight dimensions (blocks t, t + TPR, ...; two
 // 16-byte loads each, all in flight at once), smooths them once, reduces the
-// row statistics over the block and quantises from its registers. One pass
-// over HBM, the smoothing division done once per element. Results are
-// identical to quant_rows_kernel (same per-element recipe; the row sums add
-// exact integers, so their order does not matter).
-template <int R, int NB>
+// row statistics over the row's threads and quantises from its registers.
+// One pass over HBM, the smoothing division done once per element. Rows of
+// more than 32 blocks take a whole block (TPR = 256); shorter rows 8, 16 or
+// 32 threads and one block of eight dimensions each (NB = 1), 256 / TPR rows
+// per block, so that the block's boundary table serves all of them and no
+// thread idles on a 64-long row (the rows of one block lie in one 256-row
+// tile, hence in one row level). Results are identical to quant_rows_kernel
+// (same per-element recipe; the row sums add exact integers, so their order
+// does not matter).
+template <int R, int NB, int TPR>
 __global__ void __launch_bounds__(256) quant_row_cta_kernel(QuantArgs q) {
+  static_assert(TPR == 256 || (NB == 1 && TPR >= 8 && TPR <= 32), "short rows: 8 to 32 threads, one block each");
+  constexpr int RPB = 256 / TPR;  // rows per block
   __shared__ int s_bnd[kBndTab];
   __shared__ float s_red[3][8];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int row = blockIdx.x;
+  const int sub = tid % TPR;  // the thread's place in its row
+  const int row = blockIdx.x * RPB + tid / TPR;
+  const bool in_range = row < q.rows;
   const float qf = (float)q.q;
-  int src = row;
+  int src = in_range ? row : -1;
   LevelQ lq{q.ratio, q.G, q.vcap, q.ktab, q.amap};
   if (q.row_of) {
-    src = __ldg(q.row_of + row);
+    src = in_range ? __ldg(q.row_of + row) : -1;
+    const int tile = (blockIdx.x * RPB) >> 8;  // the block's rows' tile
     int lv = q.nlev - 1;
     for (int l = 0; l < q.nlev; ++l)
-      if ((row >> 8) < __ldg(q.lev_tile0 + l + 1)) {
+      if (tile < __ldg(q.lev_tile0 + l + 1)) {
         lv = l;
         break;
       }
@@ -451,38 +519,44 @@ __global__ void __launch_bounds__(256) quant_row_cta_kernel(QuantArgs q) {
   const bool use_tab = q.q + 1 < kBndTab;
   if (use_tab)
     for (int i = tid; i <= q.q + 1; i += 256) s_bnd[i] = bnd_of<R>(lq, (float)i, qf);
+  __syncthreads();  // the boundary table is complete
   const int nb = d8(q.d);
   int16_t* out = q.out16;
-  if (src < 0) {  // padding row of a level's last tile: a zero operand
-    for (int jb = tid; jb < nb; jb += 256)
+  if (in_range && src < 0) {  // padding row of a level's last tile: a zero operand
+    for (int jb = sub; jb < nb; jb += TPR)
       *reinterpret_cast<uint4*>(out + blk_idx(q.rows, row, 8 * jb)) = make_uint4(0, 0, 0, 0);
-    if (tid == 0) {
+    if (sub == 0) {
       if (q.row_scale) q.row_scale[row] = 0.f;
       if (q.row_zp) q.row_zp[row] = 0.f;
       if (q.row_sum) q.row_sum[row] = 0.f;
     }
-    return;  // uniform over the block: no barrier follows for it
   }
+  // a thread of a padding or out-of-range row takes part in its row group's
+  // shuffles with zeros and stores nothing; a whole-block row leaves at once
+  // (uniform over the block: no barrier follows for it)
+  const bool active = in_range && src >= 0;
+  if (TPR == 256 && !active) return;
   float xs[NB][8];
 #pragma unroll
   for (int k = 0; k < NB; ++k) {
-    const int j0 = 8 * (tid + 256 * k);
-    if (q.vec && j0 + 8 <= q.d) {
+    const int j0 = 8 * (sub + TPR * k);
+    if (active && q.vec && j0 + 8 <= q.d) {
       const float4* sp = reinterpret_cast<const float4*>(q.x + (size_t)src * q.d + j0);
       const float4 u = __ldg(sp), w = __ldg(sp + 1);
       xs[k][0] = u.x; xs[k][1] = u.y; xs[k][2] = u.z; xs[k][3] = u.w;
       xs[k][4] = w.x; xs[k][5] = w.y; xs[k][6] = w.z; xs[k][7] = w.w;
     } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) xs[k][e] = j0 + e < q.d ? __ldg(q.x + (size_t)src * q.d + j0 + e) : 0.f;
+      for (int e = 0; e < 8; ++e)
+        xs[k][e] = active && j0 + e < q.d ? __ldg(q.x + (size_t)src * q.d + j0 + e) : 0.f;
     }
   }
-  if (q.smooth) {
+  if (q.smooth && active) {
 #pragma unroll
     for (int k = 0; k < NB; ++k)
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const int j = 8 * (tid + 256 * k) + e;
+        const int j = 8 * (sub + TPR * k) + e;
         if (j < q.d) {
           const float sv = __ldg(q.smooth + j);
           xs[k][e] = q.smooth_div ? fdiv(xs[k][e], sv) : fmul(xs[k][e], sv);
@@ -497,29 +571,40 @@ __global__ void __launch_bounds__(256) quant_row_cta_kernel(QuantArgs q) {
     for (int k = 0; k < NB; ++k)
 #pragma unroll
       for (int e = 0; e < 8; ++e)
-        if (8 * (tid + 256 * k) + e < q.d) {
+        if (8 * (sub + TPR * k) + e < q.d) {
           const float x = xs[k][e];
           am = fmaxf(am, fabsf(x));
           mx = fmaxf(mx, x);
           mn = fminf(mn, x);
         }
-    am = warp_max(am);
-    mx = warp_max(mx);
-    mn = warp_min(mn);
-    if (lane == 0) {
-      s_red[0][warp] = am;
-      s_red[1][warp] = mx;
-      s_red[2][warp] = mn;
-    }
-    __syncthreads();
-    am = s_red[0][0];
-    mx = s_red[1][0];
-    mn = s_red[2][0];
+    if constexpr (TPR == 256) {
+      am = warp_max(am);
+      mx = warp_max(mx);
+      mn = warp_min(mn);
+      if (lane == 0) {
+        s_red[0][warp] = am;
+        s_red[1][warp] = mx;
+        s_red[2][warp] = mn;
+      }
+      __syncthreads();
+      am = s_red[0][0];
+      mx = s_red[1][0];
+      mn = s_red[2][0];
 #pragma unroll
-    for (int w = 1; w < 8; ++w) {
-      am = fmaxf(am, s_red[0][w]);
-      mx = fmaxf(mx, s_red[1][w]);
-      mn = fminf(mn, s_red[2][w]);
+      for (int w = 1; w < 8; ++w) {
+        am = fmaxf(am, s_red[0][w]);
+        mx = fmaxf(mx, s_red[1][w]);
+        mn = fminf(mn, s_red[2][w]);
+      }
+    } else {
+      // the row's TPR lanes (an aligned group of the warp): xor offsets below
+      // TPR stay inside it
+#pragma unroll
+      for (int o = TPR / 2; o > 0; o >>= 1) {
+        am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+        mn = fminf(mn, __shfl_xor_sync(0xFFFFFFFFu, mn, o));
+      }
     }
     if (R == Q_GROUP_ASYM) {
       sc = fdiv(fmaxf(fsub(mx, mn), 1e-5f), qf);
@@ -527,12 +612,11 @@ __global__ void __launch_bounds__(256) quant_row_cta_kernel(QuantArgs q) {
     } else {
       sc = fdiv(fmaxf(am, 1e-5f), qf);
     }
-    if (tid == 0) {
+    if (sub == 0 && active) {
       q.row_scale[row] = sc;
       if (R == Q_GROUP_ASYM) q.row_zp[row] = zp;
     }
-  } else {
-    __syncthreads();  // the boundary table is complete
+  } else if (active) {
     if (R == Q_TENSOR_BIP || R == Q_TENSOR_UNI) {
       inv = __ldg(q.params + q.param_off);
       zp = R == Q_TENSOR_UNI ? __ldg(q.params + q.param_off + 2) : 0.f;
@@ -545,36 +629,44 @@ __global__ void __launch_bounds__(256) quant_row_cta_kernel(QuantArgs q) {
   }
   const int* tab = use_tab ? s_bnd : nullptr;
   float rsum = 0.f;
+  if (active) {
 #pragma unroll
-  for (int k = 0; k < NB; ++k) {
-    const int jb = tid + 256 * k;
-    if (jb >= nb) break;
-    const int j0 = 8 * jb;
-    uint32_t packed[4] = {0u, 0u, 0u, 0u};
+    for (int k = 0; k < NB; ++k) {
+      const int jb = sub + TPR * k;
+      if (jb >= nb) break;
+      const int j0 = 8 * jb;
+      uint32_t packed[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int j = j0 + e;
-      int16_t code = 0;
-      if (j < q.d) code = quant_one<R>(q, lq, j, xs[k][e], sc, inv, zp, qf, rsum, tab);
-      packed[e >> 1] |= (uint32_t)(uint16_t)code << (16 * (e & 1));
+      for (int e = 0; e < 8; ++e) {
+        const int j = j0 + e;
+        int16_t code = 0;
+        if (j < q.d) code = quant_one<R>(q, lq, j, xs[k][e], sc, inv, zp, qf, rsum, tab);
+        packed[e >> 1] |= (uint32_t)(uint16_t)code << (16 * (e & 1));
+      }
+      *reinterpret_cast<uint4*>(out + blk_idx(q.rows, row, j0)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
     }
-    *reinterpret_cast<uint4*>(out + blk_idx(q.rows, row, j0)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
   }
   if (q.row_sum) {
-    rsum = warp_sum(rsum);
-    __syncthreads();  // every thread has read s_red
-    if (lane == 0) s_red[0][warp] = rsum;
-    __syncthreads();
-    if (tid == 0) {
-      float t = 0.f;
-      for (int w = 0; w < 8; ++w) t = fadd(t, s_red[0][w]);
-      q.row_sum[row] = t;
+    if constexpr (TPR == 256) {
+      rsum = warp_sum(rsum);
+      __syncthreads();  // every thread has read s_red
+      if (lane == 0) s_red[0][warp] = rsum;
+      __syncthreads();
+      if (tid == 0) {
+        float t = 0.f;
+        for (int w = 0; w < 8; ++w) t = fadd(t, s_red[0][w]);
+        q.row_sum[row] = t;
+      }
+    } else {
+#pragma unroll
+      for (int o = TPR / 2; o > 0; o >>= 1) rsum = fadd(rsum, __shfl_xor_sync(0xFFFFFFFFu, rsum, o));
+      if (sub == 0 && active) q.row_sum[row] = rsum;
     }
   }
 }
 
-// Blocks of eight dimensions per thread of quant_row_cta_kernel for d (0:
-// rows too long, quant_rows_kernel instead).
+// Blocks of eight dimensions per thread of a whole-block row of
+// quant_row_cta_kernel for d (0: rows too long, quant_rows_kernel instead).
 static int row_cta_blocks(int d) {
   const int nb = d8(d);
   for (int k = 1; k <= 8; k *= 2)
@@ -584,11 +676,20 @@ static int row_cta_blocks(int d) {
 
 template <int R>
 static cudaError_t launch_row_cta(const QuantArgs& q, cudaStream_t st) {
-  switch (row_cta_blocks(q.d)) {
-    case 1: quant_row_cta_kernel<R, 1><<<q.rows, 256, 0, st>>>(q); break;
-    case 2: quant_row_cta_kernel<R, 2><<<q.rows, 256, 0, st>>>(q); break;
-    case 4: quant_row_cta_kernel<R, 4><<<q.rows, 256, 0, st>>>(q); break;
-    default: quant_row_cta_kernel<R, 8><<<q.rows, 256, 0, st>>>(q); break;
+  const int nb = d8(q.d);
+  if (nb <= 8) {
+    quant_row_cta_kernel<R, 1, 8><<<cdiv(q.rows, 32), 256, 0, st>>>(q);
+  } else if (nb <= 16) {
+    quant_row_cta_kernel<R, 1, 16><<<cdiv(q.rows, 16), 256, 0, st>>>(q);
+  } else if (nb <= 32) {
+    quant_row_cta_kernel<R, 1, 32><<<cdiv(q.rows, 8), 256, 0, st>>>(q);
+  } else {
+    switch (row_cta_blocks(q.d)) {
+      case 1: quant_row_cta_kernel<R, 1, 256><<<q.rows, 256, 0, st>>>(q); break;
+      case 2: quant_row_cta_kernel<R, 2, 256><<<q.rows, 256, 0, st>>>(q); break;
+      case 4: quant_row_cta_kernel<R, 4, 256><<<q.rows, 256, 0, st>>>(q); break;
+      default: quant_row_cta_kernel<R, 8, 256><<<q.rows, 256, 0, st>>>(q); break;
+    }
   }
   count_launch();
   return cudaGetLastError();
@@ -681,6 +782,15 @@ cudaError_t launch_group_params(const float* stats, int batch, int rpb, int G, i
   if (ng > 0) {
     group_params_kernel<<<ng, 256, 0, st>>>(stats, rpb, recipe == GP_HEAD ? rpb : G, q,
                                                        recipe, scale, zp);
+    count_launch();
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_head_params(const QuantArgs& q, int batch, int q_max, float* scale, float* inv,
+                               cudaStream_t st) {
+  if (batch > 0) {
+    head_params_kernel<<<batch, 512, 0, st>>>(q, q_max, scale, inv);
     count_launch();
   }
   return cudaGetLastError();

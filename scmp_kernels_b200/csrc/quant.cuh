@@ -62,6 +62,10 @@ struct QuantArgs {
 cudaError_t launch_row_stats(const QuantArgs& q, float* stats, cudaStream_t st);
 cudaError_t launch_group_params(const float* stats, int batch, int rpb, int G, int q, int recipe,
                                 float* scale, float* zp, cudaStream_t st);
+// Per batch entry (rows_per_batch rows of q.x): scale and its inverse of the
+// per_head recipe, in one pass.
+cudaError_t launch_head_params(const QuantArgs& q, int batch, int q_max, float* scale, float* inv,
+                               cudaStream_t st);
 cudaError_t launch_tensor_params(const float* sa, int ra, const float* sb, int rb, int d, int q,
                                  int unipolar, const double* ranges, float* scal, cudaStream_t st);
 cudaError_t launch_quant_rows(int recipe, const QuantArgs& q, cudaStream_t st);

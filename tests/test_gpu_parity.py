@@ -136,6 +136,23 @@ def test_random_vs_oracle(case, impl, env_vars):
     assert np.array_equal(y, ref), f"max |diff| {np.abs(y - ref).max()}"
 
 
+@pytest.mark.parametrize("smooth", [False, True])
+def test_per_head_one_pass_params_vs_oracle(smooth, impl, env_vars):
+    """per_head scales from the one-pass head kernel: heads that start off a
+    16-byte boundary (odd d), an all-zero head on each side, with and without
+    SmoothQuant scales, against the oracle bit for bit."""
+    env_vars({})
+    g = torch.Generator().manual_seed(77)
+    a = (torch.randn(4, 31, 13, generator=g) * 2).numpy()
+    b = (torch.randn(4, 17, 13, generator=g) * 0.5).numpy()
+    a[2] = 0.0
+    b[1] = 0.0
+    s = (torch.rand(13, generator=g) + 0.5).numpy() if smooth else None
+    y = _run(a, b, dict(granularity="per_head", sc_prec=8), s)
+    ref = O.sc_matmul(a, b, "per_head", sc_prec=8, smooth_scales=s, env={})
+    assert np.array_equal(y, ref), f"max |diff| {np.abs(y - ref).max()}"
+
+
 @pytest.mark.parametrize("shape,kw", [
     ((300, 520, 1000), dict(granularity="per_row", sc_prec=8)),
     ((700, 1300, 512), dict(granularity="per_row", mode="unipolar", sc_prec=6, stoc_len=64)),
@@ -232,6 +249,14 @@ def test_band_grouped_tile_order_matches_default(shape, kw, group, monkeypatch, 
     ((33, 90, 130), dict(granularity="per_tensor", mode="unipolar", sc_prec=7)),
     ((3, 40, 50, 64), dict(granularity="per_head", sc_prec=8)),
     ((2, 9, 140, 31), dict(granularity="per_row", sc_prec=8)),                           # 3D per_row
+    # short rows: 8, 16 or 32 threads per row, several rows per block, the
+    # last block partly past the rows
+    ((70, 33, 64), dict(granularity="per_row", mode="unipolar", sc_prec=6, stoc_len=64)),
+    ((45, 37, 100), dict(granularity="per_row", mode="unipolar", sc_prec=6, stoc_len=64, smooth=True)),
+    ((77, 50, 256), dict(granularity="per_row", sc_prec=8, group_a=3, group_b=7)),
+    ((61, 29, 200), dict(granularity="per_row", mode="unipolar", sc_prec=7, group_a=2, group_b=5)),
+    ((3, 197, 64, 197), dict(granularity="per_head", sc_prec=8)),
+    ((5, 197, 197, 64), dict(granularity="per_head", sc_prec=8)),
 ])
 def test_row_block_quantiser_matches_warp_quantiser(shape, kw, monkeypatch, env_vars):
     """The default quantiser (one block per row, the row in registers, one

@@ -87,6 +87,9 @@ CASES = [
     (270, 300, 384, [64, 64, 64], [64, 48, 32], dict(mode="unipolar", sc_prec=6, group_b=3)),
     (600, 128, 2048, [256, 128], "stoc_len", dict(mode="bipolar", sc_prec=8)),  # long tiles: wide kernel
     (40, 90, 96, [128, 256, 64, 512], None, dict(mode="bipolar", sc_prec=9, chunk_d=32)),
+    # short rows (several rows per quantiser block, padding rows among them)
+    (330, 70, 120, [64, 256], None, dict(mode="unipolar", sc_prec=8, group_b=3)),
+    (270, 300, 64, [256, 128], "stoc_len", dict(mode="bipolar", sc_prec=8)),
 ]
 
 
