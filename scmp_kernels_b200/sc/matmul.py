@@ -138,26 +138,39 @@ def _sc_matmul_impl(
                                                   chunk_d=chunk_d, **kw)
                 return _sc_matmul_per_row(x, y, group_a=group_a, group_b=group_b, mode=mode, **kw)
             if _host_pipelined_applies(a, b):
-                return _per_row_host_pipelined(a, b, per_row_2d, group_a, group_b)
+                if smooth_scales is not None and smooth_scales.device.type != "cuda":
+                    # on the device before the operands' copies are queued:
+                    # host-to-device copies run in the order they are issued,
+                    # so a copy issued inside the first block's call would wait
+                    # for all of a's and b's (config 5: first GEMM at 22 ms
+                    # instead of 5.5 ms)
+                    kw["smooth_scales"] = smooth_scales.to(torch.device("cuda", torch.cuda.current_device()))
+                L = stoc_len if stoc_len is not None else 2 ** sc_prec
+                return _per_row_host_pipelined(a, b, per_row_2d, group_a, group_b, L)
             return per_row_2d(a, b)
         return _sc_matmul_per_row_batched(a, b, group_a=group_a, group_b=group_b, mode=mode, **kw)
     return _sc_matmul_per_head_bipolar(a, b, **kw)
 
 
-# Host operands: the rows of a are processed in three blocks, a quarter, a
-# half and a quarter of the rows. The first block runs against b's row blocks
-# as they arrive (b is copied to the device block by block on a copy stream
-# while the previous block computes); the later blocks run against the whole
-# of b (the middle one is one call, so that fewer, larger GEMMs run; the last
-# one is a quarter, so that little result is left to copy back after the last
-# GEMM). Each finished block of result rows (contiguous in memory) is copied
-# back on a second copy stream while the next block computes. Applies to 2D
-# per_row calls with both operands in pinned host memory and a CUDA device
-# present; per_row quantisation is row-local (row groups are kept whole), so
-# the blocks give the same bits as one call.
-_HOST_A_FIRST = 4         # the first block is 1/_HOST_A_FIRST of a's rows, and so is the last
-_HOST_B_BLOCKS = 4        # blocks of b's rows in the first pass
-_HOST_MIN_ROWS = 1024     # smaller calls are not split
+# Host operands: the rows of a are processed in three blocks. The first block
+# runs against b's row blocks as they arrive (b is copied to the device block
+# by block on a copy stream while the previous block computes); the later
+# blocks run against the whole of b (the middle one is one call, so that
+# fewer, larger GEMMs run; the last one is a third of the rest, so that little
+# result is left to copy back after the last GEMM). Each finished block of
+# result rows (contiguous in memory) is copied back on a second copy stream
+# while the next block computes. The first block is sized so that its GEMM
+# against one b block takes about as long as that block's copy: r rows against
+# c rows of b cost 2*r*c*D*L tensor ops (about 6.5e15 per s) and the copy
+# 4*c*D bytes (about 55e9 per s), equal at r = 2^18 / L rows (1024 at L = 256,
+# a quarter of config 2's a; 4096 at L = 64, half of config 5's), at least a
+# quarter and at most half of a, in whole 256-row tiles. Applies to 2D per_row
+# calls with both operands in pinned host memory and a CUDA device present;
+# per_row quantisation is row-local (row groups are kept whole), so the blocks
+# give the same bits as one call.
+_HOST_FIRST_ROWS_L = 1 << 18  # first block's rows times the stream length
+_HOST_B_BLOCKS = 4            # blocks of b's rows in the first pass
+_HOST_MIN_ROWS = 1024         # smaller calls are not split
 
 
 def _host_pipelined_applies(a: torch.Tensor, b: torch.Tensor) -> bool:
@@ -171,12 +184,30 @@ def _blocks(total: int, step: int, unit: int):
     return [(r, min(total, r + step)) for r in range(0, total, step)]
 
 
-def _per_row_host_pipelined(a: torch.Tensor, b: torch.Tensor, run, group_a: int, group_b: int) -> torch.Tensor:
+def _a_blocks(n: int, L: int, group_a: int):
+    """Row ranges of a's blocks (first, middle, last); inner boundaries on
+    whole row groups."""
+    tile = 256
+
+    def up(x, k):
+        return -(-x // k) * k
+
+    first = up(max(1, _HOST_FIRST_ROWS_L // max(1, L)), tile)
+    first = up(min(max(first, (n + 3) // 4), (n + 1) // 2), group_a)
+    if first >= n:
+        return [(0, n)]
+    b2 = up(n - up((n - first) // 3, tile), group_a)  # start of the last block
+    if b2 <= first or b2 >= n:
+        return [(0, first), (first, n)]
+    return [(0, first), (first, b2), (b2, n)]
+
+
+def _per_row_host_pipelined(a: torch.Tensor, b: torch.Tensor, run, group_a: int, group_b: int,
+                            L: int = 256) -> torch.Tensor:
     from . import kernels as K
     dev = torch.device("cuda", torch.cuda.current_device())
     n, m = a.shape[0], b.shape[0]
-    q = _blocks(n, (n + _HOST_A_FIRST - 1) // _HOST_A_FIRST, group_a)  # quarters
-    a_blocks = [q[0], (q[1][0], q[-2][1]), q[-1]] if len(q) > 3 else q
+    a_blocks = _a_blocks(n, L, group_a)
     b_blocks = _blocks(m, (m + _HOST_B_BLOCKS - 1) // _HOST_B_BLOCKS, group_b)
     comp = torch.cuda.current_stream(dev)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)

@@ -314,20 +314,24 @@ def test_result_scattered_to_several_buffers(gran, shape, simt, monkeypatch, env
 
 @pytest.mark.parametrize("kw", [dict(sc_prec=8), dict(sc_prec=6, mode="unipolar", stoc_len=64, group_b=7),
                                 dict(sc_prec=8, chunk_d=64, stoc_len=128, rng_levels=128),
-                                dict(sc_prec=8, group_a=5), dict(sc_prec=6, mode="unipolar", stoc_len=32, group_a=3)])
+                                dict(sc_prec=8, group_a=5), dict(sc_prec=6, mode="unipolar", stoc_len=32, group_a=3),
+                                dict(sc_prec=6, mode="unipolar", stoc_len=64, smooth=True)])
 def test_host_operands_pipelined_equal_device_result(kw, env_vars):
     """Pinned host operands take the streamed path (b and the result moved in
-    blocks while blocks compute); the result equals the device call's."""
+    blocks while blocks compute); the result equals the device call's. With
+    SmoothQuant scales in pinned host memory too."""
     env_vars({})
     from scmp_kernels_b200.sc import matmul as MM
+    kw = dict(kw)
     g = torch.Generator().manual_seed(4)
     m = MM._HOST_MIN_ROWS + 333
     a = torch.randn(MM._HOST_MIN_ROWS + 77, 256, generator=g).pin_memory()
     b = (torch.randn(m, 256, generator=g) * 0.05).pin_memory()
+    s = (torch.rand(256, generator=g) + 0.5).pin_memory() if kw.pop("smooth", False) else None
     assert MM._host_pipelined_applies(a, b)
-    y_host = sc_matmul(a, b, "per_row", **kw)
+    y_host = sc_matmul(a, b, "per_row", smooth_scales=s, **kw)
     assert y_host.device.type == "cpu" and y_host.shape == (a.shape[0], m)
-    y_dev = sc_matmul(a.to(DEV), b.to(DEV), "per_row", **kw)
+    y_dev = sc_matmul(a.to(DEV), b.to(DEV), "per_row", smooth_scales=s.to(DEV) if s is not None else None, **kw)
     assert torch.equal(y_host, y_dev.cpu())
     assert _lib.device_error() == 0
 

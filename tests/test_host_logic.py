@@ -146,3 +146,23 @@ def test_sobol_config_builders_match_fixture_configs(name, build):
     import json
     z = np.load(os.path.join(GOLDEN, name + ".npz"))
     assert json.loads(str(z["params"]))["config"] == build()
+
+
+@pytest.mark.parametrize("n,L,g", [(4096, 256, 1), (8192, 64, 1), (1101, 256, 5), (1101, 64, 3),
+                                   (1024, 32, 1), (12608, 256, 4), (2000, 128, 7), (1024, 512, 1)])
+def test_host_pipeline_row_blocks(n, L, g):
+    """a's blocks on the streamed host path: they tile [0, n) in order, inner
+    boundaries fall on whole row groups, the first block is 2^18 / L rows in
+    whole 256-row tiles, between a quarter and half of a (config 2: a quarter;
+    config 5, L = 64: half)."""
+    from scmp_kernels_b200.sc.matmul import _a_blocks
+    bl = _a_blocks(n, L, g)
+    assert bl[0][0] == 0 and bl[-1][1] == n
+    assert all(x[1] == y[0] and x[0] < x[1] for x, y in zip(bl, bl[1:]))
+    assert all(x[1] % g == 0 for x in bl[:-1])
+    first = bl[0][1]
+    assert (n + 3) // 4 <= first <= (n + 1) // 2 + g
+    if (n, L) == (4096, 256):
+        assert bl == [(0, 1024), (1024, 3072), (3072, 4096)]
+    if (n, L) == (8192, 64):
+        assert first == 4096
