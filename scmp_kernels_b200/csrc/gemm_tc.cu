@@ -1120,13 +1120,15 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
         if (lane == 0) mbar_arrive_leader<PAIR>(acce_bar(buf), rank);
         continue;
       }
-      // Wide tiles always have one accumulation unit (the chunked path and
-      // short tiles run on the two-buffer kernel), so the wide kernel's code
-      // needs no chunk epilogue: without it the default wide kernel spills
-      // 8 bytes of registers instead of 24 (the 128-register limit of 512
-      // threads). The row-level wide kernel keeps it (it compiles without
-      // spills with it, with spills without it)
-      const bool chunked = (LEV || !C::WIDE) && ep.kind == EPI_CHUNK;
+      // The chunk epilogue is compiled only into the kernels that can run it:
+      // wide tiles always have one accumulation unit, and with e2m1 operands
+      // the chunked path runs on the unrolled two-buffer kernel (UNR), the
+      // short tiles on the rolled one. Without it the default wide kernel
+      // spills 8 bytes of registers instead of 24 and the short-tile kernel
+      // none instead of 68 (the 128-register limit of 512 / 416 threads). The
+      // row-level kernels keep it (the wide one compiles without spills with
+      // it, with spills without it)
+      const bool chunked = (LEV || (!C::WIDE && (!C::F4 || UNR))) && ep.kind == EPI_CHUNK;
       for (int u = 0; u < sc.nunits; ++u, ++uc) {
         const int buf = (int)(uc % nbuf);
         if (!mbar_wait(accf_bar(buf), (uc / nbuf) & 1, abort_flag, 5)) goto epi_out;
