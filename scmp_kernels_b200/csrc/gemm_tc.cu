@@ -1042,7 +1042,13 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
       }
       const int ia = a0 + (int)rank * C::BM + 32 * q + lane;
       const int m_end = min(g.m, b0 + sc.tile_b);  // end of this tile's columns
-      if (wk.part >= 0) {
+      // Tail pieces (stream-K) come only to kernels that can receive them: the
+      // row-level launcher runs whole tiles, and the unrolled two-buffer e2m1
+      // kernel runs the chunked path (several accumulation units, no tail)
+      // and the opt-in narrow long tiles (no tail either); without this code
+      // those kernels do not spill (76 and 72 bytes with it)
+      constexpr bool TAIL_CODE = !LEV && !(C::F4 && !C::WIDE && UNR);
+      if (TAIL_CODE && wk.part >= 0) {
         // ---- one K piece of a tail tile
         const int buf = (int)(uc % nbuf);
         if (!mbar_wait(accf_bar(buf), (uc / nbuf) & 1, abort_flag, 5)) goto epi_out;
@@ -1390,7 +1396,10 @@ static Sched make_sched(int batch, int n, int m, int d, int unit_d, Variant v, i
   s.workers = s.tiles < units ? s.tiles : units;
   const int rem = s.tiles % units;
   const char* off = getenv("SCMP_TC_NO_SPLIT");
-  if (s.nunits == 1 && rem > 0 && !(off && off[0] == '1')) {
+  // (e2m1 narrow long tiles, an opt-in comparison mode, run on the unrolled
+  // two-buffer kernel, which is compiled without the tail; so do row levels)
+  const bool narrow_long = v.f4 && !v.wide && v.long_tiles;
+  if (s.nunits == 1 && rem > 0 && !(off && off[0] == '1') && !narrow_long) {
     const size_t part_bytes = (size_t)(pair ? 2 : 1) * 128 * tmax * sizeof(int);
     const long long tblk = (long long)rem * s.nblk;
     long long tw = units;

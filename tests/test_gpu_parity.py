@@ -154,6 +154,27 @@ def test_per_head_one_pass_params_vs_oracle(smooth, impl, env_vars):
 
 
 @pytest.mark.parametrize("shape,kw", [
+    ((600, 1100, 1024), dict(granularity="per_row", sc_prec=8)),                       # 512 stages per tile
+    ((530, 700, 4096), dict(granularity="per_row", mode="unipolar", sc_prec=6, stoc_len=64)),
+])
+def test_narrow_long_tiles_equal_default(shape, kw, monkeypatch, env_vars):
+    """The opt-in narrow kernel for long tiles (SCMP_TC_NARROW=1: 240-wide
+    tiles on the unrolled two-buffer kernel, whole tiles only) gives the
+    default wide kernel's bits."""
+    env_vars({})
+    monkeypatch.setattr(K, "_FORCE_SIMT", False)
+    n, m, d = shape
+    g = torch.Generator(device=DEV).manual_seed(21)
+    a = torch.randn(n, d, device=DEV, generator=g)
+    b = torch.randn(m, d, device=DEV, generator=g) * 0.03
+    y_wide = sc_matmul(a, b, **kw)
+    monkeypatch.setenv("SCMP_TC_NARROW", "1")
+    y_narrow = sc_matmul(a, b, **kw)
+    assert torch.equal(y_wide, y_narrow)
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("shape,kw", [
     ((300, 520, 1000), dict(granularity="per_row", sc_prec=8)),
     ((700, 1300, 512), dict(granularity="per_row", mode="unipolar", sc_prec=6, stoc_len=64)),
     ((260, 600, 640), dict(granularity="per_row", sc_prec=8, chunk_d=64, stoc_len=128, rng_levels=128)),
