@@ -841,7 +841,9 @@ __device__ __forceinline__ bool produce(const GemmArgs& g, const Sched& sc, uint
 // LEV: row levels (GemmArgs.nlev > 0): every a tile belongs to one level,
 // whose stream length (TLEN is then unused), b operand, tables and epilogue
 // scale the item uses; tiles past the last level are skipped by every role.
-template <int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE, bool F4, bool UNR, bool LEV = false>
+// TAIL = false: the launch has no stream-K tail (Sched.tail_w == 0), so the
+// tail pieces' epilogue is not compiled in.
+template <int TLEN, int SPD, bool PAIR, bool ATMEM, bool WIDE, bool F4, bool UNR, bool LEV = false, bool TAIL = true>
 __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_tc_kernel(GemmArgs g, Sched sc) {
   using C = Cfg<PAIR, ATMEM, WIDE, F4>;
   constexpr int NST = C::NST;
@@ -1047,7 +1049,7 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
       // kernel runs the chunked path (several accumulation units, no tail)
       // and the opt-in narrow long tiles (no tail either); without this code
       // those kernels do not spill (76 and 72 bytes with it)
-      constexpr bool TAIL_CODE = !LEV && !(C::F4 && !C::WIDE && UNR);
+      constexpr bool TAIL_CODE = TAIL && !LEV && !(C::F4 && !C::WIDE && UNR);
       if (TAIL_CODE && wk.part >= 0) {
         // ---- one K piece of a tail tile
         const int buf = (int)(uc % nbuf);
@@ -1258,10 +1260,10 @@ __global__ void __launch_bounds__(Cfg<PAIR, ATMEM, WIDE, F4>::THREADS, 1) gemm_t
 }
 
 template <int TLEN, int SPD, bool PAIR, bool ATMEM = false, bool WIDE = ATMEM && wide_tiles<TLEN>(), bool F4 = false,
-          bool UNR = F4 && WIDE, bool LEV = false>
+          bool UNR = F4 && WIDE, bool LEV = false, bool TAIL = true>
 static cudaError_t launch_t(const GemmArgs& g, const Sched& s, int sms, cudaStream_t st) {
   using C = Cfg<PAIR, ATMEM, WIDE, F4>;
-  auto kern = gemm_tc_kernel<TLEN, SPD, PAIR, ATMEM, WIDE, F4, UNR, LEV>;
+  auto kern = gemm_tc_kernel<TLEN, SPD, PAIR, ATMEM, WIDE, F4, UNR, LEV, TAIL>;
   // The attribute belongs to the current device's context, so it is set on
   // every launch (a host call; a process may drive several devices).
   {
@@ -1399,7 +1401,12 @@ static Sched make_sched(int batch, int n, int m, int d, int unit_d, Variant v, i
   // (e2m1 narrow long tiles, an opt-in comparison mode, run on the unrolled
   // two-buffer kernel, which is compiled without the tail; so do row levels)
   const bool narrow_long = v.f4 && !v.wide && v.long_tiles;
-  if (s.nunits == 1 && rem > 0 && !(off && off[0] == '1') && !narrow_long) {
+  // A last wave at least 90% full is run as whole tiles: sharing it saves at
+  // most a tenth of a tile and its fix-ups cost more (config 2, 72 tiles on
+  // 74 pairs: GEMM 11.31 ms split, 11.23 ms whole; config 5, 70 on 74:
+  // 34.07 / 34.02 ms)
+  const bool worth = (long long)rem * 10 <= (long long)units * 9;
+  if (s.nunits == 1 && rem > 0 && worth && !(off && off[0] == '1') && !narrow_long) {
     const size_t part_bytes = (size_t)(pair ? 2 : 1) * 128 * tmax * sizeof(int);
     const long long tblk = (long long)rem * s.nblk;
     long long tw = units;
@@ -1460,6 +1467,14 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t st) {
     }
   }
   if (v.f4) {  // e2m1 operands: TLEN is the padded stream length, 64 .. 512
+    if (v.wide && s.tail_w == 0) {  // whole tiles only: the kernel without the tail's code
+      switch (g.lp) {
+        case 64: return launch_t<64, 1, true, false, true, true, true, false, false>(g, s, sms, st);
+        case 128: return launch_t<128, 1, true, false, true, true, true, false, false>(g, s, sms, st);
+        case 256: return launch_t<256, 1, true, false, true, true, true, false, false>(g, s, sms, st);
+        default: return launch_t<512, 1, true, false, true, true, true, false, false>(g, s, sms, st);
+      }
+    }
     if (v.wide) {
       switch (g.lp) {
         case 64: return launch_t<64, 1, true, false, true, true>(g, s, sms, st);

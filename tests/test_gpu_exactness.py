@@ -9,8 +9,9 @@
   odd increments (checked against the C restatement of the reference's
   accumulator, sc/kernels.py:216-252).
 * The full-size benchmark outputs at their far corners (the last output
-  tiles, which the stream-K tail of the default GEMM computes in pieces)
-  against the CPU oracle.
+  tiles: whole tiles for config 2, whose last wave fills 72 of 74 SM pairs;
+  pieces of the stream-K tail for config 2 with 10048 rows of b and for
+  config 5's 512-row run) against the CPU oracle.
 * enable_matmul on quantised operands, per_tensor 3D (kernels.py:1207-1226)
   and the SC_OWEN_MODE=random masks against the reference's own function on
   the same CUDA device (kernels.py:646-704; the reference installed in
@@ -99,18 +100,21 @@ def test_mixed_sign_accumulator_past_2p22_vs_c_oracle(variant):
     assert _lib.device_error() == 0
 
 
-@pytest.mark.parametrize("workload", ["config2", "config5"])
+@pytest.mark.parametrize("workload", ["config2", "config2_tail", "config5"])
 def test_full_size_far_corner_vs_oracle(workload, monkeypatch):
-    """The last 64 x 64 block of the full config-2 output and of config 5's
-    512-row run (the last output tiles of the default GEMM's schedule, which
-    its stream-K tail shares over SM pairs) equal the CPU oracle's."""
+    """The last 64 x 64 block of the full config-2 output (its last wave is
+    whole tiles), of config 2 with 10048 rows of b (336 tiles: a last wave of
+    40 tiles that the stream-K tail shares over the 74 SM pairs) and of
+    config 5's 512-row run (a tail as well) equal the CPU oracle's."""
     for k in ("SC_OWEN_MODE", "SC_DISABLE_OWEN", "SC_SCRAMBLE_RESCALE", "SCMP_TC_INT8", "SCMP_TC_ATMEM",
               "SCMP_TC_SINGLE"):
         monkeypatch.delenv(k, raising=False)
     monkeypatch.setattr(K, "_FORCE_SIMT", False)
     from scmp_kernels_b200 import workloads as W
-    if workload == "config2":
+    if workload.startswith("config2"):
         a, b = W.config2(DEV)
+        if workload == "config2_tail":
+            b = b[:10048].contiguous()
         kw = dict(mode="bipolar", sc_prec=8)
         s = None
     else:
