@@ -144,20 +144,32 @@ class ClockSampler:
         P, h = self.P, self.h
         while not self._stop.is_set():
             try:
+                # SM clock and throttle reasons only: with the board power read
+                # in the same loop, the first step's launches were held up
+                # (1 run in 40 against 0 in 40 without it, 2 bench runs in 9)
                 sm = float(P.nvmlDeviceGetClockInfo(h, P.NVML_CLOCK_SM))
                 rs = int(P.nvmlDeviceGetCurrentClocksEventReasons(h))
-                pw = P.nvmlDeviceGetPowerUsage(h) / 1000.0
-                self.samples.append((sm, self.max_mhz, pw, [n for n, b in self.bits.items() if rs & b]))
+                self.samples.append((sm, self.max_mhz, None, [n for n, b in self.bits.items() if rs & b],
+                                     time.perf_counter()))
             except Exception:  # noqa: BLE001
                 pass
             self._stop.wait(self.period)
 
     def start(self):
+        """Start sampling and return once the first sample is in: the
+        sampler's first driver queries then happen before the timed region
+        opens. (Started just before the region, they delayed the host's first
+        launches in about one run in four while the GPU's queue was empty:
+        4-12 ms of idle GPU at the first step.)"""
         self.samples = []
+        self._t_open = None
         self._stop.clear()
         if self.kind == "nvml":
             self._thread = threading.Thread(target=self._loop, daemon=True)
             self._thread.start()
+            t0 = time.time()
+            while not self.samples and time.time() - t0 < 2.0:
+                time.sleep(0.002)
             return
         import tempfile
         self._file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False).name
@@ -173,6 +185,11 @@ class ClockSampler:
         t0 = time.time()  # let the sampler start before the timed region
         while self._proc is not None and time.time() - t0 < 10 and os.path.getsize(self._file) == 0:
             time.sleep(0.05)
+
+    def mark(self):
+        """The timed region opens now: samples taken before are dropped (while
+        one at least falls inside the region)."""
+        self._t_open = time.perf_counter()
 
     def stop(self):
         if self.kind == "nvml":
@@ -196,12 +213,20 @@ class ClockSampler:
             os.unlink(self._file)
         if not self.samples:
             return None
+        if self.kind == "nvml" and self._t_open is not None:
+            inside = [x for x in self.samples if x[4] >= self._t_open]
+            if inside:
+                self.samples = inside
         mx = self.samples[-1][1]
         sms = [s[0] for s in self.samples]
         load = [s for s in sms if mx and s > 0.5 * mx] or sms
         reasons = sorted({r for s in self.samples for r in s[3]})
-        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(sms), "power_w_max": max(s[2] for s in self.samples), "sampler": self.kind}
+        out = {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": reasons,
+               "samples": len(sms), "sampler": self.kind}
+        power = [s[2] for s in self.samples if s[2] is not None]
+        if power:
+            out["power_w_max"] = max(power)
+        return out
 
 
 # ---------------------------------------------------------------------------
@@ -350,14 +375,16 @@ def measure(name, shape, args, rank, world, dev, sampler=None, check_rows=128):
     for e0, e1 in gev + qev:  # torch creates the CUDA event on first record
         e0.record()
         e1.record()
+    if sampler is not None:  # running (first sample taken) before the region opens
+        sampler.start()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    if sampler is not None:
-        sampler.start()
     t0, t1 = mk(), mk()
     launches0 = _lib.launch_count()
+    if sampler is not None:
+        sampler.mark()
     t0.record()
     ei = 0
     for _ in range(args.steps):
